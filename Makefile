@@ -1,0 +1,41 @@
+# FlashGANN-B200 build.
+#
+#   make gpu_flashgann [EXTRA_NVFLAGS="-DINTERNAL_TOPK=1024"]   -> bin/gpu_flashgann (+ the library)
+#   make lib                                                  -> flashgann_b200/libflashgann.so
+#   make oracle                                               -> oracle/liboracle.so (test infrastructure)
+#
+# Same knobs as the reference Makefile (ARCH, EXTRA_NVFLAGS); this build
+# targets sm_100a only.
+NVCC    ?= nvcc
+ARCH    ?= sm_100a
+GENCODE := -gencode arch=compute_100a,code=$(ARCH)
+NVFLAGS := -std=c++17 -O3 $(GENCODE) -lineinfo -Xptxas -v $(EXTRA_NVFLAGS)
+CSRC    := flashgann_b200/csrc
+LIB     := flashgann_b200/libflashgann.so
+BIN_DIR := bin
+
+KERNEL_SRC := $(CSRC)/fg_kernels.cu $(CSRC)/fg_api.cu
+HEADERS    := $(CSRC)/fg_config.h $(CSRC)/fg_internal.h include/flashgann.h
+
+.PHONY: all lib gpu_flashgann oracle clean
+
+all: lib gpu_flashgann
+
+lib: $(LIB)
+
+$(LIB): $(KERNEL_SRC) $(HEADERS)
+	$(NVCC) $(NVFLAGS) -Xcompiler -fPIC -shared -o $@ $(KERNEL_SRC) 2> $(CSRC)/ptxas.log || (cat $(CSRC)/ptxas.log; exit 1)
+
+$(BIN_DIR):
+	mkdir -p $(BIN_DIR)
+
+gpu_flashgann: $(BIN_DIR)/gpu_flashgann
+
+$(BIN_DIR)/gpu_flashgann: $(CSRC)/fg_cli.cpp $(LIB) | $(BIN_DIR)
+	$(CXX) -std=c++17 -O2 $(EXTRA_NVFLAGS) -o $@ $(CSRC)/fg_cli.cpp -L$(dir $(LIB)) -lflashgann -Wl,-rpath,'$$ORIGIN/../flashgann_b200'
+
+oracle:
+	$(MAKE) -C oracle
+
+clean:
+	rm -f $(LIB) $(BIN_DIR)/gpu_flashgann $(CSRC)/ptxas.log

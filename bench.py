@@ -1,0 +1,347 @@
+"""FlashGANN-B200 benchmark: QPS at recall@100 >= 0.95 on the 1M x 128,
+degree-32 seeded synthetic config.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl flashgann|reference]
+
+One step = one search of the config's 10,000-query batch at the smallest beam
+of the config's beam list whose recall@100 reaches 0.95 (calibrated before
+timing, untimed).  Each rank searches its own full batch on its own GPU with
+the index replicated (queries partition, no collective on the data path:
+weak scaling); rank 0 prints one JSON line.
+
+--impl reference runs the reference's algorithm on the host cores (the C
+oracle port with OpenMP; the reference itself has no CPU path) on a bounded
+sample, and additionally times the reference's own sm_100a build
+(oracle/_ref, QuantizationGraph::gpu_search_adaptive) on the same batch.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+TARGET_RECALL = 0.95
+
+
+def _dist():
+    import torch
+    import torch.distributed as dist
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1 and not dist.is_initialized():
+        import datetime
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo",
+                                timeout=datetime.timedelta(seconds=900))
+    return ws, rank, local
+
+
+def _barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def _max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) < 9:
+                    continue
+                try:
+                    sm.append(float(p[1]))
+                    mx.append(float(p[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, p[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic_per_query():
+    """DRAM bytes per query from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "search_kernel_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return None
+
+
+def _calibrate(run, gt, K, beams):
+    """Smallest beam of the config list reaching the target recall."""
+    import flashgann_b200 as fg
+    table = []
+    for beam in beams:
+        ids = run(beam)
+        r = fg.compute_recall(ids, gt, K)
+        table.append((beam, r))
+        if r >= TARGET_RECALL:
+            return beam, r, table
+    return beams[-1], table[-1][1], table
+
+
+def cpu_baseline(ds, beam, budget_s=12.0, threads=0):
+    """The oracle port (C, OpenMP over queries) on a bounded sample."""
+    import oracle
+    oi = oracle.OracleIndex(ds.rows, ds.signs, ds.entry, ds.spec.dim, ds.spec.degree)
+    cores = threads or os.cpu_count() or 1
+    probe = min(len(ds.queries), max(8, cores))
+    t0 = time.perf_counter()
+    oi.search(ds.queries[:probe], ds.spec.K, beam, threads=cores)
+    dt = time.perf_counter() - t0
+    n = int(min(len(ds.queries), max(probe, budget_s / max(dt, 1e-6) * probe)))
+    t0 = time.perf_counter()
+    ids, _ = oi.search(ds.queries[:n], ds.spec.K, beam, threads=cores)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "queries/s", "cores": cores, "kind": "port",
+            "sample": f"first {n} of {len(ds.queries)} queries at beam {beam}, {dt:.1f} s on {cores} threads"}, ids
+
+
+def run_flashgann(args, ws, rank, local):
+    import torch
+    import flashgann_b200 as fg
+    from flashgann_b200 import builder
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    # rank 0 materialises the dataset (cached under _data/); the others read it
+    if rank == 0:
+        ds = builder.materialize(args.config, device=dev, verbose=True)
+    _barrier(ws)
+    if rank != 0:
+        ds = builder.materialize(args.config, device=dev)
+    spec = ds.spec
+    K, nq = spec.K, len(ds.queries)
+    qg = fg.QuantizationGraph(spec.n, spec.dim, spec.degree, ds.codebook_path, device=local)
+    dq = torch.from_numpy(ds.queries).to(dev)
+    dout = torch.empty((nq, K), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def run_dev(beam):
+        qg.search_device(dq, K, beam, d_out=dout, stream=stream)
+        torch.cuda.synchronize()
+        return dout.cpu().numpy().view(np.uint32)
+
+    beam, recall, table = (args.beam, None, []) if args.beam else _calibrate(run_dev, ds.gt, K, spec.beams)
+    if recall is None:
+        recall = fg.compute_recall(run_dev(beam), ds.gt, K)
+    # counters of one pass (traversal is deterministic) for the roofline
+    dstats = torch.zeros((nq, 4), dtype=torch.int32, device=dev)
+    qg.search_device(dq, K, beam, d_out=dout, stream=stream, d_stats=dstats)
+    torch.cuda.synchronize()
+    st = dstats.cpu().numpy().astype(np.int64)
+    evals, expans = int(st[:, 2].sum()), int(st[:, 1].sum())
+    L = builder.layout(spec.dim, spec.degree)
+    graded_bytes = evals * (spec.dim * 4 + spec.degree * L.padded_dim // 8 + spec.degree * 4)
+    refined_bytes = evals * spec.dim * 4 + expans * spec.degree * (L.padded_dim // 8 + 4 + 12)
+
+    for _ in range(args.warmup):
+        qg.search_device(dq, K, beam, d_out=dout, stream=stream)
+    torch.cuda.synchronize()
+    _barrier(ws)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            qg.search_device(dq, K, beam, d_out=dout, stream=stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    _barrier(ws)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_max = _max_over_ranks(ms, ws)
+    clocks = clk.summary()
+
+    # end to end through the public host-buffer API (pinned host memory)
+    hq = torch.from_numpy(ds.queries).pin_memory().numpy()
+    hres = torch.empty((nq, K), dtype=torch.int32).pin_memory().numpy().view(np.uint32)
+    for _ in range(max(1, args.warmup // 2)):
+        qg.gpu_search_adaptive(nq, hq, K, hres, beam)
+    _barrier(ws)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        qg.gpu_search_adaptive(nq, hq, K, hres, beam)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    e2e_max = _max_over_ranks(e2e_s, ws)
+    qg.close()
+
+    value = ws * nq / (ms_max / 1e3)
+    peak, peak_kind = _peaks()
+    achieved = graded_bytes / (ms / 1e3) / 1e9
+    traffic = _traffic_per_query()
+    out = {
+        "metric": "QPS @ recall@100=0.95 (1M x 128, deg 32)",
+        "value": value, "unit": "queries/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded 200-component GMM, BASELINE.json configs[1])",
+        "config": {"workload": spec.name, "n": spec.n, "dim": spec.dim, "degree": spec.degree, "K": K,
+                   "queries_per_gpu": nq, "beam": beam, "recall_at_k": recall,
+                   "recall_table": table, "parallelism": f"queries partitioned, index replicated x{ws}",
+                   "l2": "inputs larger than L2 (codebook %.2f GB > 126 MB)" % (spec.n * L.row * 4 / 1e9)},
+        "e2e": {"value": ws * nq / e2e_max, "unit": "queries/s",
+                "h2d_bytes_per_step": nq * spec.dim * 4, "d2h_bytes_per_step": nq * K * 4},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "traffic": (traffic["dram_bytes_per_query"] * nq if traffic else None),
+                     "algorithmic_bytes_per_step": graded_bytes, "refined_bytes_per_step": refined_bytes,
+                     "visited_per_query": evals / nq, "expanded_per_query": expans / nq},
+        "clocks": clocks,
+    }
+    if rank == 0 and not args.no_cpu:
+        out["cpu_baseline"], _ = cpu_baseline(ds, beam, budget_s=args.cpu_seconds)
+    return out
+
+
+def run_reference(args, ws, rank, local):
+    from flashgann_b200 import builder
+    import flashgann_b200 as fg
+    if rank != 0:
+        return None
+    import torch
+    dev = f"cuda:{local}" if torch.cuda.is_available() else "cpu"
+    ds = builder.materialize(args.config, device=dev, verbose=True)
+    spec = ds.spec
+    K, nq = spec.K, len(ds.queries)
+    extra = {}
+    beam = args.beam
+    try:
+        from oracle import ref
+        if ref.available() and torch.cuda.is_available():
+            g = ref.RefGraph(ds.codebook_path, spec.n, spec.dim, spec.degree)
+            if not beam:
+                beam, _, _ = _calibrate(lambda b: g.search(ds.queries, K, b)[0], ds.gt, K, spec.beams)
+            ids, _ = g.search(ds.queries, K, beam)
+            times = []
+            for _ in range(max(1, args.steps)):
+                t0 = time.perf_counter()
+                ids, el = g.search(ds.queries, K, beam)
+                times.append((el, time.perf_counter() - t0))
+            g.close()
+            el = statistics.median(t[0] for t in times)
+            call = statistics.median(t[1] for t in times)
+            extra["reference_gpu"] = {
+                "what": "reference sm_100a build, QuantizationGraph::gpu_search_adaptive, 1 GPU",
+                "value": nq / el, "unit": "queries/s", "beam": beam,
+                "recall_at_k": fg.compute_recall(ids, ds.gt, K) if os.path.exists(fg._capi.LIB_PATH) else None,
+                "elapsed_s": el, "call_s_including_index_upload": call}
+    except Exception as e:  # the CPU leg below is the contract's reference arm
+        extra["reference_gpu"] = {"unavailable": f"{type(e).__name__}: {e}"}
+    if not beam:
+        beam = spec.beams[-1]
+    steps = []
+    for _ in range(max(1, args.steps)):
+        cb, _ = cpu_baseline(ds, beam, budget_s=args.cpu_seconds / max(1, args.steps))
+        steps.append(cb)
+    value = statistics.median(s["value"] for s in steps)
+    cb = dict(steps[0])
+    cb["value"] = value
+    out = {
+        "impl": "reference", "metric": "QPS @ recall@100=0.95 (1M x 128, deg 32)", "value": value,
+        "unit": "queries/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE.json configs[1])",
+        "config": {"workload": spec.name, "n": spec.n, "dim": spec.dim, "degree": spec.degree, "K": K, "beam": beam},
+        "cpu_baseline": cb, "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                                    "d2h_bytes_per_step": 0},
+    }
+    out.update(extra)
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="flashgann", choices=["flashgann", "reference"])
+    ap.add_argument("--config", default="c2_1m")
+    ap.add_argument("--beam", type=int, default=0, help="fixed beam (default: calibrate to recall 0.95)")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    ws, rank, local = _dist()
+    if args.impl == "reference":
+        out = run_reference(args, ws, rank, local)
+    else:
+        out = run_flashgann(args, ws, rank, local)
+    if rank == 0 and out is not None:
+        print(json.dumps(out), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

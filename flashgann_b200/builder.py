@@ -1,0 +1,540 @@
+"""Seeded synthetic data and SymphonyQG-layout codebooks.
+
+The reference ships no index builder: its search reads a prebuilt
+"SymphonyQG-style codebook with data layout adjustment" (README.md:13) whose
+byte layout is fixed by include/qg.hpp:17-42,66-73.  This module writes files
+in exactly that layout so the reference build and this build can be run on
+identical inputs:
+
+    uint32 entry_point
+    n rows x row floats, row = [dim raw floats][deg*D/8 code bytes]
+                                [deg triple_x][deg f_dq][deg f_vq][deg uint32 ids]
+    D float signs (only the first dim are applied, include/utils.cuh:795-797)
+
+Codes and factors follow the estimator the kernel evaluates
+(include/utils.cuh:989-993): for a parent c and neighbour o, with
+u = H_D (s * pad(o - c)) (unnormalised Walsh-Hadamard, signs s), bits b = u > 0:
+
+    L2:  triple_x = |o-c|^2 + 2<o-c, c>,  f_dq = -2 |u|^2 / (D <sign(u), u>)
+    IP:  triple_x = 0,                     f_dq = -1 |u|^2 / (D <sign(u), u>)
+    f_vq = f_dq * sum(2b - 1)
+
+so that triple_x + d(q, c) + f_dq*width*(2*sum_b q - sum q) + f_vq*low
+estimates d(q, o).  Invalid neighbour slots hold id 0xFFFFFFFF and
+triple_x = FLT_MAX (the kernel's gates at adaptive_search.cuh:233,372 and
+utils.cuh:951,1000).
+
+Graph: exact k-NN, merged with reverse k-NN edges, relative-neighbourhood
+pruned and filled with the nearest pruned candidates, plus a few seeded random
+long edges per node so a single entry point reaches every mixture component.  The graph builder is offline
+test/bench infrastructure, not the search path; it uses torch (GPU when
+present) for the brute-force distance work.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import hashlib
+import math
+import os
+import struct
+from typing import Optional, Tuple
+
+import numpy as np
+import torch
+
+FLT_MAX = np.float32(3.4028234663852886e38)
+INVALID_ID = np.uint32(0xFFFFFFFF)
+
+
+# --------------------------------------------------------------------------
+# layout (include/qg.hpp:66-73)
+# --------------------------------------------------------------------------
+def padded_dim(dim: int) -> int:
+    d = 1
+    while d < dim:
+        d <<= 1
+    return d
+
+
+@dataclasses.dataclass(frozen=True)
+class Layout:
+    dim: int
+    degree: int
+    padded_dim: int
+    code_off: int
+    factor_off: int
+    nbr_off: int
+    row: int
+
+    @property
+    def code_bytes(self) -> int:
+        return self.padded_dim // 8
+
+
+def layout(dim: int, degree: int) -> Layout:
+    D = padded_dim(dim)
+    code_off = dim
+    factor_off = code_off + (D // 64) * 2 * degree
+    nbr_off = factor_off + 3 * degree
+    return Layout(dim, degree, D, code_off, factor_off, nbr_off, nbr_off + degree)
+
+
+# --------------------------------------------------------------------------
+# synthetic data
+# --------------------------------------------------------------------------
+@dataclasses.dataclass(frozen=True)
+class DatasetSpec:
+    name: str
+    n: int
+    nq: int
+    dim: int
+    n_comp: int
+    sigma: float
+    lo: float
+    hi: float
+    degree: int
+    K: int
+    beams: Tuple[int, ...]
+    seed: int
+    kind: str = "int_gmm"      # int_gmm | norm_aniso | lowrank
+    knn_k: int = 64
+    gt_k: int = 100
+
+
+SPECS = {
+    # the reference's own CPU-runnable plumbing case
+    "c1_100k": DatasetSpec("c1_100k", 100_000, 1_000, 128, 50, 20.0, 0.0, 255.0, 16, 10,
+                           (16, 32, 64, 128, 256, 512), seed=1),
+    # the headline case
+    "c2_1m": DatasetSpec("c2_1m", 1_000_000, 10_000, 128, 200, 25.0, 0.0, 255.0, 32, 100,
+                         (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=2),
+    # small cases for the parity tests (same generators, sizes the oracle finishes in seconds)
+    "t_20k": DatasetSpec("t_20k", 20_000, 200, 128, 8, 25.0, 0.0, 255.0, 32, 100,
+                         (100, 128, 256, 512, 1024), seed=11),
+    "t_8k16": DatasetSpec("t_8k16", 8_000, 200, 128, 4, 20.0, 0.0, 255.0, 16, 10,
+                          (16, 32, 64, 96, 128, 256, 512), seed=12),
+    "t_4k96f": DatasetSpec("t_4k96f", 4_000, 100, 96, 8, 0.0, 0.0, 0.0, 32, 100,
+                           (100, 256), seed=13, kind="norm_aniso"),
+    "t_2k": DatasetSpec("t_2k", 2_000, 64, 128, 4, 25.0, 0.0, 255.0, 32, 100,
+                        (32, 100, 128, 200, 256), seed=14),
+}
+
+
+def _rng(seed: int, stream: int) -> np.random.Generator:
+    return np.random.default_rng([seed, stream])
+
+
+def generate_vectors(spec: DatasetSpec) -> Tuple[np.ndarray, np.ndarray]:
+    """Base and query vectors (float32) for a spec; deterministic in the seed."""
+    if spec.kind == "int_gmm":
+        cr = _rng(spec.seed, 0)
+        centres = cr.uniform(spec.lo, spec.hi, size=(spec.n_comp, spec.dim))
+
+        def draw(stream: int, m: int) -> np.ndarray:
+            r = _rng(spec.seed, stream)
+            lab = r.integers(0, spec.n_comp, size=m)
+            out = np.empty((m, spec.dim), dtype=np.float32)
+            step = 1 << 18
+            for s in range(0, m, step):
+                e = min(m, s + step)
+                noise = r.standard_normal((e - s, spec.dim), dtype=np.float32) * np.float32(spec.sigma)
+                v = centres[lab[s:e]].astype(np.float32) + noise
+                np.rint(v, out=v)
+                np.clip(v, spec.lo, spec.hi, out=v)
+                out[s:e] = v
+            return out
+
+        return draw(1, spec.n), draw(2, spec.nq)
+    if spec.kind == "norm_aniso":
+        cr = _rng(spec.seed, 0)
+        centres = cr.standard_normal((spec.n_comp, spec.dim))
+        scales = np.exp(cr.uniform(np.log(0.05), np.log(0.5), size=(spec.n_comp, spec.dim)))
+
+        def draw(stream: int, m: int) -> np.ndarray:
+            r = _rng(spec.seed, stream)
+            lab = r.integers(0, spec.n_comp, size=m)
+            v = centres[lab] + r.standard_normal((m, spec.dim)) * scales[lab]
+            v /= np.linalg.norm(v, axis=1, keepdims=True)
+            return v.astype(np.float32)
+
+        return draw(1, spec.n), draw(2, spec.nq)
+    raise ValueError(f"unknown dataset kind {spec.kind}")
+
+
+def make_signs(D: int, seed: int) -> np.ndarray:
+    r = _rng(seed, 7)
+    return np.where(r.integers(0, 2, size=D) == 1, 1.0, -1.0).astype(np.float32)
+
+
+# --------------------------------------------------------------------------
+# exact nearest neighbours (offline, torch)
+# --------------------------------------------------------------------------
+def _device(device: Optional[str]) -> torch.device:
+    if device is None:
+        device = "cuda" if torch.cuda.is_available() else "cpu"
+    return torch.device(device)
+
+
+def _is_integer_data(x: np.ndarray) -> bool:
+    if x.size == 0:
+        return True
+    sample = x[: min(len(x), 4096)]
+    return bool(np.all(sample == np.rint(sample))) and float(np.abs(x).max()) <= 255.0
+
+
+def brute_force_knn(base: np.ndarray, queries: Optional[np.ndarray], k: int, device=None,
+                    exclude_self: bool = False, chunk: int = 0) -> Tuple[np.ndarray, np.ndarray]:
+    """Exact k nearest neighbours by squared L2, ties broken by smaller id.
+
+    Integer-valued data (|x| <= 255, the BASELINE integer configs) is searched
+    with exact integer distances; float data with fp32 distances.
+    Returns (ids int64 [m, k], d2 float64 [m, k]) sorted ascending.
+    """
+    dev = _device(device)
+    exact = _is_integer_data(base) and (queries is None or _is_integer_data(queries))
+    xb = torch.from_numpy(np.ascontiguousarray(base)).to(dev)
+    xq = xb if queries is None else torch.from_numpy(np.ascontiguousarray(queries)).to(dev)
+    n, m = xb.shape[0], xq.shape[0]
+    nb = xb.pow(2).sum(1)
+    nqv = xq.pow(2).sum(1)
+    shift = max(1, int(math.ceil(math.log2(max(n, 2)))))
+    if chunk <= 0:
+        budget = (6 << 30) if dev.type == "cuda" else (1 << 29)
+        chunk = max(16, min(m, budget // max(1, n * 12)))
+    ids_out = np.empty((m, k), dtype=np.int64)
+    d_out = np.empty((m, k), dtype=np.float64)
+    idx_all = torch.arange(n, device=dev, dtype=torch.int64)
+    for s in range(0, m, chunk):
+        e = min(m, s + chunk)
+        d = nqv[s:e, None] + nb[None, :] - 2.0 * (xq[s:e] @ xb.T)
+        d.clamp_(min=0)
+        if exclude_self:
+            r = torch.arange(s, e, device=dev)
+            d[r - s, r] = float("inf")
+        if exact:
+            key = torch.round(d).to(torch.int64)
+            if exclude_self:
+                key[r - s, r] = (1 << 62) >> shift
+            key = (key << shift) | idx_all[None, :]
+            kv, ki = torch.topk(key, k, dim=1, largest=False, sorted=True)
+            ids = kv & ((1 << shift) - 1)
+        else:
+            dv, ids = torch.topk(d, k, dim=1, largest=False, sorted=True)
+        del d
+        # recompute in float64 from the vectors and order by (distance, id)
+        qv = xq[s:e].double()
+        dd = (xb[ids].double() - qv[:, None, :]).pow(2).sum(-1)
+        order = torch.argsort(ids, dim=1, stable=True)
+        ids = torch.gather(ids, 1, order)
+        dd = torch.gather(dd, 1, order)
+        order = torch.argsort(dd, dim=1, stable=True)
+        ids_out[s:e] = torch.gather(ids, 1, order).cpu().numpy()
+        d_out[s:e] = torch.gather(dd, 1, order).cpu().numpy()
+    return ids_out, d_out
+
+
+# --------------------------------------------------------------------------
+# graph construction
+# --------------------------------------------------------------------------
+def _merge_reverse(ids: np.ndarray, d: np.ndarray, cap: int, device) -> Tuple[np.ndarray, np.ndarray]:
+    """Union of forward and reverse k-NN lists, nearest `cap` per node."""
+    dev = _device(device)
+    n, k = ids.shape
+    src = torch.arange(n, device=dev).repeat_interleave(k)
+    dst = torch.from_numpy(ids.reshape(-1)).to(dev)
+    dd = torch.from_numpy(d.reshape(-1)).to(dev)
+    node = torch.cat([src, dst])
+    cand = torch.cat([dst, src])
+    dist = torch.cat([dd, dd])
+    o = torch.argsort(cand, stable=True)
+    node, cand, dist = node[o], cand[o], dist[o]
+    o = torch.argsort(dist, stable=True)
+    node, cand, dist = node[o], cand[o], dist[o]
+    o = torch.argsort(node, stable=True)
+    node, cand, dist = node[o], cand[o], dist[o]
+    keep = torch.ones_like(node, dtype=torch.bool)
+    keep[1:] = (node[1:] != node[:-1]) | (cand[1:] != cand[:-1])
+    # (node, cand) duplicates share a distance, so they are adjacent after the sort
+    node, cand, dist = node[keep], cand[keep], dist[keep]
+    counts = torch.bincount(node, minlength=n)
+    starts = torch.cumsum(counts, 0) - counts
+    rank = torch.arange(node.numel(), device=dev) - starts[node]
+    sel = rank < cap
+    out_i = torch.full((n, cap), -1, dtype=torch.int64, device=dev)
+    out_d = torch.full((n, cap), float("inf"), dtype=torch.float64, device=dev)
+    out_i[node[sel], rank[sel]] = cand[sel]
+    out_d[node[sel], rank[sel]] = dist[sel]
+    return out_i.cpu().numpy(), out_d.cpu().numpy()
+
+
+def rng_prune(x: np.ndarray, cand: np.ndarray, cand_d: np.ndarray, R: int, alpha: float = 1.0,
+              device=None, batch: int = 0) -> np.ndarray:
+    """Relative-neighbourhood pruning of sorted candidate lists.
+
+    Candidate c of node p is dropped when a kept neighbour k has
+    alpha^2 * d(k, c) <= d(p, c) (squared distances); the list is then filled
+    to R with the nearest dropped candidates.  Returns int64 [n, R], -1 = empty.
+    """
+    dev = _device(device)
+    n, C = cand.shape
+    if batch <= 0:
+        batch = 8192 if dev.type == "cuda" else 1024
+    xt = torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    out = np.full((n, R), -1, dtype=np.int64)
+    a2 = alpha * alpha
+    for s in range(0, n, batch):
+        e = min(n, s + batch)
+        ci = torch.from_numpy(cand[s:e]).to(dev)
+        cd = torch.from_numpy(cand_d[s:e]).to(dev)
+        valid = ci >= 0
+        v = xt[ci.clamp(min=0)].double()
+        g = v @ v.transpose(1, 2)
+        sq = torch.diagonal(g, dim1=1, dim2=2)
+        pair = (sq[:, :, None] + sq[:, None, :] - 2.0 * g).clamp_(min=0)
+        B = e - s
+        kept = torch.zeros((B, C), dtype=torch.bool, device=dev)
+        count = torch.zeros(B, dtype=torch.int64, device=dev)
+        for j in range(C):
+            occl = (kept & (pair[:, :, j] * a2 <= cd[:, j:j + 1])).any(1)
+            take = valid[:, j] & ~occl & (count < R)
+            kept[:, j] = take
+            count += take.to(torch.int64)
+        # order: kept (by distance) then dropped (by distance)
+        pos = torch.arange(C, device=dev)[None, :].expand(B, C)
+        key = torch.where(kept, pos, pos + C)
+        key = torch.where(valid, key, torch.full_like(key, 3 * C))
+        order = torch.argsort(key, dim=1)[:, :R]
+        chosen = torch.gather(ci, 1, order)
+        chosen_valid = torch.gather(valid, 1, order)
+        chosen = torch.where(chosen_valid, chosen, torch.full_like(chosen, -1))
+        out[s:e, : chosen.shape[1]] = chosen.cpu().numpy()
+    return out
+
+
+def build_graph(x: np.ndarray, degree: int, seed: int, knn_k: int = 64, device=None,
+                random_links: Optional[int] = None) -> Tuple[np.ndarray, int]:
+    """Degree-`degree` neighbour lists (int64, -1 = empty) and an entry point.
+
+    Every node keeps `degree - r` relative-neighbourhood-pruned local edges and
+    `r` seeded uniformly random long edges (r = max(2, degree // 8)); the
+    entry point (the node nearest the centroid) spends half of its slots on
+    random long edges.  Without long edges a single entry point never leaves
+    its own component of a well-separated mixture.
+    """
+    n = x.shape[0]
+    k = min(knn_k, n - 1)
+    r = max(2, degree // 8) if random_links is None else random_links
+    r = min(r, degree - 1)
+    ids, d = brute_force_knn(x, None, k, device=device, exclude_self=True)
+    cand, cand_d = _merge_reverse(ids, d, cap=min(n - 1, max(96, int(1.5 * k))), device=device)
+    local = rng_prune(x, cand, cand_d, degree - r, device=device)
+    rg = _rng(seed, 5)
+    rand = (np.arange(n)[:, None] + 1 + rg.integers(0, max(1, n - 1), size=(n, r))) % n
+    nbrs = np.concatenate([local, rand], axis=1)
+    # a random target that repeats an earlier slot becomes an empty slot
+    srt = np.sort(nbrs, axis=1)
+    if np.any(srt[:, 1:] == srt[:, :-1]):
+        for i in np.nonzero(np.any((srt[:, 1:] == srt[:, :-1]) & (srt[:, 1:] >= 0), axis=1))[0]:
+            seen = set()
+            for j in range(degree):
+                v = int(nbrs[i, j])
+                if v >= 0 and v in seen:
+                    nbrs[i, j] = -1
+                seen.add(v)
+    centroid = x.astype(np.float64).mean(0)
+    d2 = np.empty(n)
+    step = 1 << 16
+    for s in range(0, n, step):
+        d2[s:s + step] = ((x[s:s + step].astype(np.float64) - centroid) ** 2).sum(1)
+    entry = int(np.argmin(d2))
+    half = degree // 2
+    extra = (entry + 1 + rg.integers(0, max(1, n - 1), size=half)) % n
+    row = [int(v) for v in local[entry] if v >= 0][: degree - half]
+    for v in extra:
+        if int(v) not in row and int(v) != entry:
+            row.append(int(v))
+    nbrs[entry] = -1
+    nbrs[entry, : len(row)] = row[:degree]
+    return nbrs, entry
+
+
+# --------------------------------------------------------------------------
+# RaBitQ encoding
+# --------------------------------------------------------------------------
+def fwht(v: torch.Tensor) -> torch.Tensor:
+    """Unnormalised Walsh-Hadamard transform over the last dim (power of two)."""
+    D = v.shape[-1]
+    shape = v.shape
+    h = 1
+    v = v.clone()
+    while h < D:
+        v = v.view(*shape[:-1], D // (2 * h), 2, h)
+        a = v[..., 0, :].clone()
+        b = v[..., 1, :]
+        v[..., 0, :] = a + b
+        v[..., 1, :] = a - b
+        v = v.view(shape)
+        h <<= 1
+    return v
+
+
+def encode_rows(x: np.ndarray, nbrs: np.ndarray, signs: np.ndarray, metric: str = "l2",
+                device=None, batch: int = 0) -> np.ndarray:
+    """Codebook rows (float32 [n, row]) in the qg_codebook layout."""
+    dev = _device(device)
+    n, dim = x.shape
+    R = nbrs.shape[1]
+    L = layout(dim, R)
+    D = L.padded_dim
+    rows = np.zeros((n, L.row), dtype=np.float32)
+    rows[:, :dim] = x
+    rows_u8 = rows.view(np.uint8)
+    rows_u32 = rows.view(np.uint32)
+    xt = torch.from_numpy(np.ascontiguousarray(x)).to(dev).double()
+    st = torch.zeros(D, dtype=torch.float64, device=dev)
+    st[:dim] = torch.from_numpy(signs[:dim]).to(dev).double()
+    scale = 2.0 if metric == "l2" else 1.0
+    if batch <= 0:
+        batch = max(1, (1 << 27) // (R * D)) if dev.type == "cuda" else max(1, (1 << 22) // (R * D))
+    bitw = torch.tensor([8, 4, 2, 1], dtype=torch.int64, device=dev)
+    for s in range(0, n, batch):
+        e = min(n, s + batch)
+        nb = torch.from_numpy(nbrs[s:e]).to(dev)
+        valid = nb >= 0
+        c = xt[s:e]                                   # [B, dim]
+        o = xt[nb.clamp(min=0)]                       # [B, R, dim]
+        diff = o - c[:, None, :]
+        u = torch.zeros((e - s, R, D), dtype=torch.float64, device=dev)
+        u[..., :dim] = diff * st[:dim]
+        u = fwht(u)
+        bits = (u > 0)
+        ip_xu = u.abs().sum(-1)
+        norm_u = u.pow(2).sum(-1)
+        fdq = torch.where(ip_xu > 0, -scale * norm_u / (D * ip_xu), torch.zeros_like(ip_xu))
+        fvq = fdq * (2.0 * bits.sum(-1).double() - D)
+        if metric == "l2":
+            tx = diff.pow(2).sum(-1) + 2.0 * (diff * c[:, None, :]).sum(-1)
+        else:
+            tx = torch.zeros_like(fdq)
+        # nibble for chunk cb: dims 4cb..4cb+3 -> bits 8,4,2,1 (include/utils.cuh:911-917)
+        nib = (bits.view(e - s, R, D // 4, 4).to(torch.int64) * bitw).sum(-1)
+        byte = (nib[..., 0::2] | (nib[..., 1::2] << 4)).to(torch.uint8)  # [B, R, D/8]
+        tx = torch.where(valid, tx, torch.full_like(tx, float(FLT_MAX)))
+        fdq = torch.where(valid, fdq, torch.zeros_like(fdq))
+        fvq = torch.where(valid, fvq, torch.zeros_like(fvq))
+        byte = torch.where(valid[..., None], byte, torch.zeros_like(byte))
+        cb = byte.reshape(e - s, R * (D // 8)).cpu().numpy()
+        rows_u8[s:e, L.code_off * 4: L.code_off * 4 + R * (D // 8)] = cb
+        rows[s:e, L.factor_off: L.factor_off + R] = tx.float().cpu().numpy()
+        rows[s:e, L.factor_off + R: L.factor_off + 2 * R] = fdq.float().cpu().numpy()
+        rows[s:e, L.factor_off + 2 * R: L.factor_off + 3 * R] = fvq.float().cpu().numpy()
+        ids32 = np.where(nbrs[s:e] >= 0, nbrs[s:e], 0xFFFFFFFF).astype(np.uint32)
+        rows_u32[s:e, L.nbr_off: L.nbr_off + R] = ids32
+    return rows
+
+
+def write_codebook(path: str, entry: int, rows: np.ndarray, signs: np.ndarray) -> None:
+    with open(path, "wb") as f:
+        f.write(struct.pack("<I", entry & 0xFFFFFFFF))
+        f.write(np.ascontiguousarray(rows, dtype=np.float32).tobytes())
+        f.write(np.ascontiguousarray(signs, dtype=np.float32).tobytes())
+
+
+def read_codebook(path: str, n: int, dim: int, degree: int) -> Tuple[int, np.ndarray, np.ndarray]:
+    L = layout(dim, degree)
+    with open(path, "rb") as f:
+        entry = struct.unpack("<I", f.read(4))[0]
+        rows = np.fromfile(f, dtype=np.float32, count=n * L.row).reshape(n, L.row)
+        signs = np.fromfile(f, dtype=np.float32, count=L.padded_dim)
+    return entry, rows, signs
+
+
+# --------------------------------------------------------------------------
+# fvecs / ivecs (include/data_io.hpp:18-77)
+# --------------------------------------------------------------------------
+def write_vecs(path: str, a: np.ndarray) -> None:
+    a = np.ascontiguousarray(a)
+    m, d = a.shape
+    out = np.empty((m, d + 1), dtype=np.int32)
+    out[:, 0] = d
+    out[:, 1:] = a.view(np.int32) if a.dtype in (np.float32, np.int32) else a.astype(np.int32)
+    out.tofile(path)
+
+
+def read_vecs(path: str, dtype=np.float32) -> np.ndarray:
+    raw = np.fromfile(path, dtype=np.int32)
+    if raw.size == 0:
+        return np.zeros((0, 0), dtype=dtype)
+    d = int(raw[0])
+    m = raw.size // (d + 1)
+    return raw[: m * (d + 1)].reshape(m, d + 1)[:, 1:].copy().view(dtype)
+
+
+# --------------------------------------------------------------------------
+# one-call dataset materialisation with an on-disk cache
+# --------------------------------------------------------------------------
+@dataclasses.dataclass
+class Dataset:
+    spec: DatasetSpec
+    base: np.ndarray
+    queries: np.ndarray
+    gt: np.ndarray          # int32 [nq, gt_k]
+    rows: np.ndarray        # float32 [n, row]
+    signs: np.ndarray
+    entry: int
+    layout: Layout
+    codebook_path: str
+    dir: str
+
+    def digest(self) -> str:
+        h = hashlib.sha256()
+        h.update(struct.pack("<I", self.entry))
+        h.update(self.rows.tobytes())
+        h.update(self.signs.tobytes())
+        return h.hexdigest()
+
+
+def default_cache_dir() -> str:
+    return os.environ.get("FLASHGANN_DATA", os.path.join(os.path.dirname(os.path.dirname(
+        os.path.abspath(__file__))), "_data"))
+
+
+def materialize(name_or_spec, cache_dir: Optional[str] = None, device=None,
+                verbose: bool = False) -> Dataset:
+    spec = SPECS[name_or_spec] if isinstance(name_or_spec, str) else name_or_spec
+    cache_dir = cache_dir or default_cache_dir()
+    d = os.path.join(cache_dir, spec.name)
+    os.makedirs(d, exist_ok=True)
+    L = layout(spec.dim, spec.degree)
+    paths = {k: os.path.join(d, v) for k, v in dict(
+        base="base.fvecs", query="query.fvecs", gt="gt.ivecs", cb="qg_codebook.index").items()}
+    if all(os.path.exists(p) for p in paths.values()):
+        base = read_vecs(paths["base"])
+        queries = read_vecs(paths["query"])
+        gt = read_vecs(paths["gt"], np.int32)
+        entry, rows, signs = read_codebook(paths["cb"], spec.n, spec.dim, spec.degree)
+        return Dataset(spec, base, queries, gt, rows, signs, entry, L, paths["cb"], d)
+    import time
+    t0 = time.time()
+    base, queries = generate_vectors(spec)
+    if verbose:
+        print(f"[builder] {spec.name}: vectors {time.time() - t0:.1f}s", flush=True)
+    nbrs, entry = build_graph(base, spec.degree, spec.seed, knn_k=spec.knn_k, device=device)
+    if verbose:
+        print(f"[builder] {spec.name}: graph {time.time() - t0:.1f}s", flush=True)
+    signs = make_signs(L.padded_dim, spec.seed)
+    rows = encode_rows(base, nbrs, signs, device=device)
+    if verbose:
+        print(f"[builder] {spec.name}: codes {time.time() - t0:.1f}s", flush=True)
+    gt_ids, _ = brute_force_knn(base, queries, min(spec.gt_k, spec.n), device=device)
+    gt = gt_ids.astype(np.int32)
+    tmp = paths["cb"] + ".tmp"
+    write_codebook(tmp, entry, rows, signs)
+    write_vecs(paths["base"], base)
+    write_vecs(paths["query"], queries)
+    write_vecs(paths["gt"], gt)
+    os.replace(tmp, paths["cb"])
+    if verbose:
+        print(f"[builder] {spec.name}: done {time.time() - t0:.1f}s", flush=True)
+    return Dataset(spec, base, queries, gt, rows, signs, entry, L, paths["cb"], d)

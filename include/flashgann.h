@@ -1,0 +1,153 @@
+/*
+ * flashgann.h -- C ABI of the B200 FlashGANN search engine (libflashgann.so).
+ *
+ * Drop-in boundary for the reference's search path (SophiaSun18/FlashGANN):
+ * plain pointers and sizes, no C++ or torch types, every failure returned as
+ * a status code instead of the reference's exit()/throw.  Each entry point
+ * names the reference interface it replaces (file:line in that project).
+ *
+ * Threading: an fg_index may be used by one host thread at a time.
+ * Devices: every call runs on the device the index was created on and
+ * restores the caller's current device before returning.
+ */
+#ifndef FLASHGANN_H
+#define FLASHGANN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (the reference exits or throws instead) ---- */
+#define FG_OK 0
+#define FG_ERR_IO 1          /* file cannot be opened or is short      (qg.hpp:22-23 throws) */
+#define FG_ERR_FORMAT 2      /* codebook/vecs content inconsistent     (data_io.hpp:41 asserts) */
+#define FG_ERR_ARG 3         /* invalid argument                       */
+#define FG_ERR_CUDA 4        /* CUDA runtime error                     (utils.cuh:42-50 exits) */
+#define FG_ERR_OOM 5         /* not enough device memory               (gpu_search_adaptive.cu:61-63 throws) */
+#define FG_ERR_UNSUPPORTED 6 /* outside this build's supported envelope */
+#define FG_ERR_NO_DEVICE 7   /* no CUDA device / product kernels not loadable */
+
+/* ---- metric (include/metric.hpp:9) ---- */
+#define FG_METRIC_L2 0
+#define FG_METRIC_IP 1
+
+typedef struct fg_index fg_index;
+
+/* Codebook layout in float words, as QuantizationGraph's getters report it
+ * (include/qg.hpp:49-60,66-73). */
+typedef struct fg_layout {
+    uint64_t num_nodes;
+    uint64_t dim;
+    uint64_t padded_dim;
+    uint64_t code_offset;
+    uint64_t factor_offset;
+    uint64_t neighbor_offset;
+    uint64_t row_offset;
+    int32_t degree;
+    uint32_t entry_point; /* resolved: the centroid fallback already applied */
+    int32_t metric;
+    int32_t device;
+} fg_layout;
+
+/* Per-query counters written by fg_search_device_ex (all optional). */
+typedef struct fg_query_stats {
+    uint32_t iterations;  /* loop iterations that merged candidates into the beam */
+    uint32_t expansions;  /* parents expanded (neighbour lists read) */
+    uint32_t evaluations; /* exact distances computed, entry point included */
+    uint32_t estimates;   /* RaBitQ estimates computed */
+} fg_query_stats;
+
+const char* fg_status_string(int status);
+/* Message of the last failure on the calling thread ("" if none). */
+const char* fg_last_error(void);
+
+/* Replaces QuantizationGraph::QuantizationGraph(n, dim, degree, path)
+ * (include/qg.hpp:17-42) together with the index upload of
+ * QuantizationGraph::gpu_search_adaptive (gpu_search_adaptive.cu:46-77):
+ * reads the qg_codebook file, resolves entry point UINT32_MAX to the node
+ * nearest the centroid (include/common.hpp:26-47), checks free memory and
+ * keeps the codebook resident on `device` until fg_index_free. */
+int fg_index_load(const char* path, uint64_t num_nodes, uint64_t dim, int32_t degree, int32_t metric,
+                  int32_t device, fg_index** out);
+
+/* Same, from a codebook already in host memory: rows[num_nodes*row_offset]
+ * and signs[padded_dim] in the qg_codebook layout. */
+int fg_index_create(const float* rows, const float* signs, uint32_t entry_point, uint64_t num_nodes,
+                    uint64_t dim, int32_t degree, int32_t metric, int32_t device, fg_index** out);
+
+/* Replaces ~QuantizationGraph (include/qg.hpp:44-47). NULL is accepted. */
+int fg_index_free(fg_index* index);
+
+/* Replaces the layout getters (include/qg.hpp:49-60). */
+int fg_index_layout(const fg_index* index, fg_layout* out);
+
+/* Replaces QuantizationGraph::set_metric (include/qg.hpp:54). */
+int fg_index_set_metric(fg_index* index, int32_t metric);
+
+/* Replaces QuantizationGraph::gpu_search_adaptive(nq, queries, K, result_idx,
+ * beam_sz, elapsed) (gpu_search_adaptive.cu:12-114): host buffers in and out,
+ * synchronous.  queries[nq*dim] row-major fp32, result_idx[nq*K].
+ * elapsed_s (optional) = wall time of the search launch and its
+ * synchronisation, excluding the copies, as the reference measures it
+ * (gpu_search_adaptive.cu:98-107).  Supported: 1 <= K, 1 <= beam <= 1024,
+ * degree <= 32, dim <= 4096. */
+int fg_search(fg_index* index, int32_t nq, const float* queries, int32_t K, uint32_t* result_idx, int32_t beam,
+              double* elapsed_s);
+
+/* Device-resident variant: d_queries / d_result_idx / d_result_dist (optional)
+ * are device pointers on the index's device; the call is asynchronous on
+ * `stream` (a cudaStream_t, NULL = default stream). */
+int fg_search_device(fg_index* index, int32_t nq, const float* d_queries, int32_t K, uint32_t* d_result_idx,
+                     float* d_result_dist, int32_t beam, void* stream);
+
+/* Extended device variant: optional per-query counters d_stats[nq] and an
+ * optional traversal trace d_trace[nq*trace_cap*8] (expander node ids per
+ * iteration, 0xFFFFFFFF when unused) with d_trace_count[nq*trace_cap]. */
+int fg_search_device_ex(fg_index* index, int32_t nq, const float* d_queries, int32_t K, uint32_t* d_result_idx,
+                        float* d_result_dist, int32_t beam, void* stream, fg_query_stats* d_stats,
+                        uint32_t* d_trace, int32_t* d_trace_count, int32_t trace_cap);
+
+/* Query-side rotation and quantisation (include/utils.cuh:790-939) as a
+ * standalone kernel: per query the rotated vector d_rotated[nq*D], the 6-bit
+ * codes d_quant[nq*D], the 16-entry nibble LUT d_lut[nq*4*D] and
+ * d_factors[nq*3] = (low, high, width), d_sum_q[nq].  Any output may be NULL
+ * except d_factors. */
+int fg_query_prepare_device(const float* d_queries, int32_t nq, int32_t dim, const float* d_signs,
+                            float* d_rotated, uint8_t* d_quant, uint8_t* d_lut, float* d_factors,
+                            int32_t* d_sum_q, void* stream);
+
+/* Beam merge primitive on device, for verification (include/utils.cuh:1369-1399):
+ * ncase independent cases, each [itopk beam entries | cbs candidates] in
+ * d_idx/d_dist, merged in place with the reference's tie order. */
+int fg_beam_merge_device(uint32_t* d_idx, float* d_dist, int32_t ncase, int32_t itopk, int32_t cbs, int32_t first,
+                         void* stream);
+
+/* ---- host helpers of the reference CLI ---- */
+
+/* include/utils.cuh:119-127 */
+uint32_t fg_effective_sort_beam_size(uint32_t beam);
+
+/* include/common.hpp:49-66: recall of predicted[nq*topk] against
+ * groundtruth[nq*gt_k]; duplicates in a prediction row are all counted. */
+float fg_compute_recall(const uint32_t* predicted, const int32_t* groundtruth, uint64_t nq, int32_t topk,
+                        int32_t gt_k);
+
+/* include/common.hpp:68-94: append TopK,Beam_size,Runtime,Latency,Throughput,Recall. */
+int fg_append_run_stats_csv(const char* path, int32_t k, int32_t beam, double runtime, double latency,
+                            double throughput, double recall);
+
+/* include/metric.hpp:13-28: FG_METRIC_IP iff the path contains "text2image1m". */
+int32_t fg_infer_metric_from_path(const char* path);
+
+/* include/data_io.hpp:18-77: count and dim of an fvecs/ivecs file
+ * (count = file_size / (4 + 4*dim)), then read it into dst[count*dim]. */
+int fg_vecs_info(const char* path, uint64_t* count, int32_t* dim);
+int fg_vecs_read(const char* path, void* dst, uint64_t count, int32_t dim);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
