@@ -14,8 +14,8 @@ CSRC    := flashgann_b200/csrc
 LIB     := flashgann_b200/libflashgann.so
 BIN_DIR := bin
 
-KERNEL_SRC := $(CSRC)/fg_kernels.cu $(CSRC)/fg_api.cu
-HEADERS    := $(CSRC)/fg_config.h $(CSRC)/fg_internal.h include/flashgann.h
+KERNEL_SRC := $(CSRC)/fg_search.cu $(CSRC)/fg_api.cu
+HEADERS    := $(CSRC)/fg_config.h $(CSRC)/fg_internal.h $(CSRC)/fg_device.cuh include/flashgann.h
 
 .PHONY: all lib gpu_flashgann oracle clean
 

@@ -109,6 +109,10 @@ SPECS = {
     # the headline case
     "c2_1m": DatasetSpec("c2_1m", 1_000_000, 10_000, 128, 200, 25.0, 0.0, 255.0, 32, 100,
                          (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=2),
+    # the headline config's per-component structure (5,000 points per component, degree 32)
+    # at a fifth of the size, for profiling captures that must stay small
+    "p_200k": DatasetSpec("p_200k", 200_000, 2_000, 128, 40, 25.0, 0.0, 255.0, 32, 100,
+                          (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=3),
     # small cases for the parity tests (same generators, sizes the oracle finishes in seconds)
     "t_20k": DatasetSpec("t_20k", 20_000, 200, 128, 8, 25.0, 0.0, 255.0, 32, 100,
                          (100, 128, 256, 512, 1024), seed=11),

@@ -42,9 +42,11 @@ struct SearchPlan {
     int merge_n2 = 0;          // 1/2/4: register bitonic merge, 0: merge path
     int mp_active = 0;         // merge-path output segments
     int vec_codes = 0;         // codes 16-byte aligned: 128-bit code loads
+    int variant = 0;           // kernel variant (warps per query, register budget)
     size_t smem_bytes = 0;
     int grid = 0;
     int threads = 0;
+    int blocks_per_sm = 0;
 };
 
 int plan_search(const SearchArgs& a, SearchPlan* plan, int device, char* err, size_t errlen);
