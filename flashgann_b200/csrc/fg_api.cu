@@ -9,6 +9,7 @@
 #include <cstring>
 #include <filesystem>
 #include <fstream>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -437,6 +438,88 @@ int fg_search(fg_index* x, int32_t nq, const float* queries, int32_t K, uint32_t
     const auto t1 = std::chrono::high_resolution_clock::now();
     if (elapsed_s) *elapsed_s = std::chrono::duration<double>(t1 - t0).count();
     if ((e = cudaMemcpyAsync(result_idx, x->d_results, rn * sizeof(uint32_t), cudaMemcpyDeviceToHost, x->stream)) != cudaSuccess)
+        return cuda_fail(e, "cudaMemcpyAsync(results)");
+    if ((e = cudaStreamSynchronize(x->stream)) != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    return FG_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Scratch of fg_search_noalloc: the work counter, the staged queries and the
+// staged result ids of one call, all in this fixed array instead of buffers
+// from cudaMalloc.  Every call on a device uses the same array, so it holds
+// the previous call's data until the next call overwrites it.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[FG_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxScratchDevices] = {};
+
+// Address of g_noalloc_scratch on `device` (which must be current), looked
+// up once per device by the first fg_search_noalloc call there.
+int noalloc_scratch(int device, unsigned char** out) {
+    if (device < 0 || device >= kMaxScratchDevices)
+        return fail(FG_ERR_UNSUPPORTED, "fg_search_noalloc supports devices 0..%d (got %d)", kMaxScratchDevices - 1, device);
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_ptr[device]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
+        g_scratch_ptr[device] = p;
+    }
+    *out = static_cast<unsigned char*>(g_scratch_ptr[device]);
+    return FG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fg_search_noalloc(fg_index* x, int32_t nq, const float* queries, int32_t K, uint32_t* result_idx, int32_t beam,
+                      double* elapsed_s) {
+    g_err.clear();
+    if (!x) return fail(FG_ERR_ARG, "null index");
+    if (nq < 0) return fail(FG_ERR_ARG, "nq must be >= 0 (got %d)", nq);
+    if (nq > 0 && (!queries || !result_idx)) return fail(FG_ERR_ARG, "null query or result buffer");
+    if (elapsed_s) *elapsed_s = 0.0;
+    DeviceGuard g(x->device);
+    if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
+    fg::SearchArgs a = base_args(x);
+    a.nq = nq;
+    a.K = K;
+    a.beam = beam;
+    fg::SearchPlan plan;
+    char err[256];
+    int rc = fg::plan_search(a, &plan, x->device, err, sizeof(err));
+    if (rc) return fail(rc, "%s", err);
+    // scratch layout: [work counter | queries nq*dim | result ids nq*K], 256-byte aligned parts
+    const size_t qbytes = static_cast<size_t>(nq) * x->dim * sizeof(float);
+    const size_t rbytes = static_cast<size_t>(nq) * K * sizeof(uint32_t);
+    const size_t q_off = 256, r_off = q_off + ((qbytes + 255) & ~size_t(255));
+    if (r_off + rbytes > FG_NOALLOC_SCRATCH_BYTES)
+        return fail(FG_ERR_ARG,
+                    "fg_search_noalloc: %d queries of dim %llu with K=%d need %zu bytes of scratch, above its fixed "
+                    "%d bytes; split the batch or call fg_search",
+                    nq, static_cast<unsigned long long>(x->dim), K, r_off + rbytes, FG_NOALLOC_SCRATCH_BYTES);
+    unsigned char* s = nullptr;
+    if ((rc = noalloc_scratch(x->device, &s)) != FG_OK) return rc;
+    if (nq == 0) return FG_OK;
+    a.work_counter = reinterpret_cast<uint32_t*>(s);
+    a.queries = reinterpret_cast<const float*>(s + q_off);
+    a.out_ids = reinterpret_cast<uint32_t*>(s + r_off);
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(s + q_off, queries, qbytes, cudaMemcpyHostToDevice, x->stream)) != cudaSuccess)
+        return cuda_fail(e, "cudaMemcpyAsync(queries)");
+    if ((e = cudaStreamSynchronize(x->stream)) != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    const auto t0 = std::chrono::high_resolution_clock::now();
+    // launch_search zeroes the work counter on the stream before the kernel
+    if ((e = fg::launch_search(a, plan, x->stream)) != cudaSuccess) return cuda_fail(e, "search launch");
+    if ((e = cudaStreamSynchronize(x->stream)) != cudaSuccess) return cuda_fail(e, "search");
+    const auto t1 = std::chrono::high_resolution_clock::now();
+    if (elapsed_s) *elapsed_s = std::chrono::duration<double>(t1 - t0).count();
+    if ((e = cudaMemcpyAsync(result_idx, s + r_off, rbytes, cudaMemcpyDeviceToHost, x->stream)) != cudaSuccess)
         return cuda_fail(e, "cudaMemcpyAsync(results)");
     if ((e = cudaStreamSynchronize(x->stream)) != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
     return FG_OK;

@@ -97,6 +97,29 @@ int fg_index_set_metric(fg_index* index, int32_t metric);
 int fg_search(fg_index* index, int32_t nq, const float* queries, int32_t K, uint32_t* result_idx, int32_t beam,
               double* elapsed_s);
 
+/* Size of the fixed device scratch used by fg_search_noalloc (8 MiB). */
+#define FG_NOALLOC_SCRATCH_BYTES 8388608
+
+/* fg_search without any device allocation; it has no counterpart in the
+ * reference.  Same arguments, results and errors as fg_search, but the
+ * queries, the result ids and the kernel's work counter are staged in a fixed
+ * FG_NOALLOC_SCRATCH_BYTES array of device memory that is part of the
+ * library, where fg_search grows buffers with cudaMalloc on demand (and the
+ * reference allocates and frees them on every call).  It is for callers that
+ * must not allocate during a search: a serving loop that must not stall its
+ * other streams on the device-wide synchronisation cudaFree implies, or a
+ * process whose device memory is entirely owned by another allocator.
+ * Limit: 256 + round_up(nq*dim*4, 256) + nq*K*4 <= FG_NOALLOC_SCRATCH_BYTES
+ * (e.g. 14,000 queries of dim 128 with K = 10); a larger batch returns
+ * FG_ERR_ARG with a message -- split it or call fg_search.
+ * The first call on each device looks up the scratch's address on that
+ * device; make that first call before any stream capture.  All calls on a
+ * device share the one scratch array: calls that overlap in time (from
+ * several threads, or on several indexes of one device) race on it and must
+ * be serialised by the caller. */
+int fg_search_noalloc(fg_index* index, int32_t nq, const float* queries, int32_t K, uint32_t* result_idx,
+                      int32_t beam, double* elapsed_s);
+
 /* Device-resident variant: d_queries / d_result_idx / d_result_dist (optional)
  * are device pointers on the index's device; the call is asynchronous on
  * `stream` (a cudaStream_t, NULL = default stream). */
