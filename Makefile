@@ -14,8 +14,10 @@ CSRC    := flashgann_b200/csrc
 LIB     := flashgann_b200/libflashgann.so
 BIN_DIR := bin
 
-KERNEL_SRC := $(CSRC)/fg_search.cu $(CSRC)/fg_api.cu
+KERNEL_SRC := $(CSRC)/fg_search.cu $(CSRC)/fg_search_warp.cu $(CSRC)/fg_api.cu
 HEADERS    := $(CSRC)/fg_config.h $(CSRC)/fg_internal.h $(CSRC)/fg_device.cuh include/flashgann.h
+OBJ_DIR    := flashgann_b200/_build
+OBJS       := $(patsubst $(CSRC)/%.cu,$(OBJ_DIR)/%.o,$(KERNEL_SRC))
 
 .PHONY: all lib gpu_flashgann oracle clean
 
@@ -23,8 +25,15 @@ all: lib gpu_flashgann
 
 lib: $(LIB)
 
-$(LIB): $(KERNEL_SRC) $(HEADERS)
-	$(NVCC) $(NVFLAGS) -Xcompiler -fPIC -shared -o $@ $(KERNEL_SRC) 2> $(CSRC)/ptxas.log || (cat $(CSRC)/ptxas.log; exit 1)
+$(OBJ_DIR)/%.o: $(CSRC)/%.cu $(HEADERS) | $(OBJ_DIR)
+	$(NVCC) $(NVFLAGS) -Xcompiler -fPIC -c -o $@ $< 2> $(OBJ_DIR)/$*.ptxas.log || (cat $(OBJ_DIR)/$*.ptxas.log; exit 1)
+
+$(OBJ_DIR):
+	mkdir -p $(OBJ_DIR)
+
+$(LIB): $(OBJS)
+	$(NVCC) $(GENCODE) -shared -o $@ $(OBJS)
+	cat $(OBJ_DIR)/*.ptxas.log > $(CSRC)/ptxas.log
 
 $(BIN_DIR):
 	mkdir -p $(BIN_DIR)
@@ -38,4 +47,4 @@ oracle:
 	$(MAKE) -C oracle
 
 clean:
-	rm -f $(LIB) $(BIN_DIR)/gpu_flashgann $(CSRC)/ptxas.log
+	rm -f $(LIB) $(BIN_DIR)/gpu_flashgann $(CSRC)/ptxas.log $(OBJS) $(OBJ_DIR)/*.ptxas.log

@@ -771,5 +771,118 @@ __device__ __forceinline__ void mp_apply(const uint32_t* sidx, const float* sdis
     }
 }
 
+// ------------------------------------------------------- parent expansion
+template <int W>
+__device__ __forceinline__ void load_codes(const float* prow, uint64_t code_off, int ni, bool vec, uint32_t (&c)[W]) {
+    const uint32_t* base = reinterpret_cast<const uint32_t*>(prow + code_off) + static_cast<size_t>(ni) * W;
+    if constexpr (W % 4 == 0) {
+        if (vec) {
+#pragma unroll
+            for (int w = 0; w < W; w += 4) {
+                const uint4 x = __ldg(reinterpret_cast<const uint4*>(base + w));
+                c[w] = x.x;
+                c[w + 1] = x.y;
+                c[w + 2] = x.z;
+                c[w + 3] = x.w;
+            }
+            return;
+        }
+    }
+#pragma unroll
+    for (int w = 0; w < W; ++w) c[w] = __ldg(base + w);
+}
+
+// One lane's slice of a parent's expansion block (neighbour `lane`).
+template <int W>
+struct ParentLane {
+    uint32_t child;
+    float tx, fdq, fvq;
+    uint32_t c[W > 0 ? W : 1];
+};
+
+// Issue every load of a parent's block for this lane: id, the three factors
+// and (for W > 0) the packed code words; nothing waits on them here.
+template <int W>
+__device__ __forceinline__ void load_parent(const float* __restrict__ prow, const SearchArgs& a, int limit, bool vec,
+                                            int lane, ParentLane<W>& p) {
+    const bool in = lane < limit;
+    const uint32_t* ids = reinterpret_cast<const uint32_t*>(prow + a.nbr_off);
+    const float* fac = prow + a.factor_off;
+    p.child = in ? __ldg(ids + lane) : kMax;
+    p.tx = in ? __ldg(fac + lane) : FLT_MAX;
+    p.fdq = in ? __ldg(fac + a.degree + lane) : 0.0f;
+    p.fvq = in ? __ldg(fac + 2 * a.degree + lane) : 0.0f;
+    if constexpr (W > 0) {
+        if (in) {
+            load_codes<W>(prow, a.code_off, lane, vec, p.c);
+        } else {
+#pragma unroll
+            for (int w = 0; w < W; ++w) p.c[w] = 0;
+        }
+    }
+}
+
+template <int W>
+__device__ __forceinline__ uint32_t parent_raw(const ParentLane<W>& p, const float* __restrict__ prow,
+                                               const SearchArgs& a, int lane, const uint32_t* planes,
+                                               const uint32_t* wrap, bool wrap_any) {
+    if constexpr (W > 0) {
+        return raw_sum<W>(p.c, planes, wrap, wrap_any);
+    } else {
+        const int Wd = a.padded_dim >> 5;
+        return raw_sum_dyn(reinterpret_cast<const uint32_t*>(prow + a.code_off) + static_cast<size_t>(lane) * Wd, Wd,
+                           planes, wrap, wrap_any);
+    }
+}
+
+// The adaptive controller's state (src/adaptive_search_utils.cuh:8-18), held
+// in warp-0 registers: every lane computes the same (warp-uniform) values.
+struct CtlRegs {
+    int theta;
+    float rho;
+    int policy_iters;
+    uint32_t top1;
+    int stall;
+    bool warmup_done;
+    float entry_d, last_d, cur_d;
+    uint32_t scan;  // merge path: beam positions before this hold expanded entries
+};
+
+// src/adaptive_search.cuh:167-190 with update_head_stall_counter,
+// update_expander_progress, apply_stage2_state and update_adaptive_state
+// (src/adaptive_search_utils.cuh:32-119).
+__device__ __forceinline__ void controller_update(CtlRegs& c, uint32_t beam0, int iter, float phase2_rho) {
+    const uint32_t top1 = beam0 & 0x7fffffffu;
+    const int stall = (c.policy_iters > 0 && top1 == c.top1) ? c.stall + 1 : 0;
+    const bool changed = c.warmup_done || stall >= TOP1_WARMUP_STALL_ITERS;
+    const float e = c.entry_d;
+    const float last = finite_lt_max(c.last_d) ? c.last_d : e;
+    const float cur = finite_lt_max(c.cur_d) ? c.cur_d : last;
+    float rate = 0.0f;
+    const float denom = fabsf(e);
+    if (isfinite(last) && isfinite(cur) && isfinite(e) && !(denom <= 1.0e-20f)) {
+        const float prog = __fdiv_rn(__fsub_rn(last, cur), denom);
+        if (isfinite(prog) && prog > 0.0f) rate = prog < 1.0f ? prog : 1.0f;
+    }
+    c.top1 = top1;
+    c.stall = stall;
+    c.last_d = last;
+    c.cur_d = cur;
+    if (changed) {
+        c.warmup_done = true;
+        c.theta = PHASE2_THETA;
+        c.rho = phase2_rho;
+        c.policy_iters += 1;
+    } else if (iter == 0 || (iter % CHECK_INTERVAL) == 0) {
+        const float span = phase2_rho > PHASE1_RHO ? __fsub_rn(phase2_rho, PHASE1_RHO) : __fsub_rn(RHO_MAX, RHO_MIN);
+        const float base = c.policy_iters == 0 ? PHASE1_RHO : c.rho;
+        const float cap = phase2_rho > PHASE1_RHO ? phase2_rho : RHO_MAX;
+        c.warmup_done = false;
+        c.theta = PHASE1_THETA;
+        c.rho = clamp_f(__fmaf_rn(span, rate, base), RHO_MIN, cap);
+        c.policy_iters += 1;
+    }
+}
+
 }  // namespace
 }  // namespace fg

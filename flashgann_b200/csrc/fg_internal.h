@@ -1,5 +1,5 @@
 // fg_internal.h -- launch interface between the C ABI (fg_api.cu) and the
-// kernels (fg_kernels.cu).  Not installed; the public surface is
+// kernels (fg_search.cu, fg_search_warp.cu).  Not installed; the public surface is
 // include/flashgann.h.
 #pragma once
 
@@ -42,7 +42,10 @@ struct SearchPlan {
     int merge_n2 = 0;          // 1/2/4: register bitonic merge, 0: merge path
     int mp_active = 0;         // merge-path output segments
     int vec_codes = 0;         // codes 16-byte aligned: 128-bit code loads
-    int variant = 0;           // kernel variant (warps per query, register budget)
+    int variant = 0;           // CTA kernel variant (warps per query, register budget)
+    int kernel = 0;            // 0: one CTA per query (fg_search.cu), 1: one warp per query (fg_search_warp.cu)
+    uint32_t slots = 0;        // warp kernel: visited-set slots
+    size_t slice_bytes = 0;    // warp kernel: shared memory per query
     size_t smem_bytes = 0;
     int grid = 0;
     int threads = 0;
@@ -51,6 +54,11 @@ struct SearchPlan {
 
 int plan_search(const SearchArgs& a, SearchPlan* plan, int device, char* err, size_t errlen);
 cudaError_t launch_search(const SearchArgs& a, const SearchPlan& plan, cudaStream_t stream);
+
+// The warp-per-query kernel (fg_search_warp.cu): padded dimensions 32..256.
+bool warp_kernel_supports(int padded_dim);
+int plan_search_warp(const SearchArgs& a, SearchPlan* plan, int device, char* err, size_t errlen);
+cudaError_t launch_search_warp(const SearchArgs& a, const SearchPlan& plan, cudaStream_t stream);
 
 cudaError_t launch_query_prepare(const float* queries, int nq, int dim, const float* signs, float* rotated,
                                  uint8_t* quant, uint8_t* lut, float* factors, int32_t* sum_q,

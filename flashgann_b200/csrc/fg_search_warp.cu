@@ -1,0 +1,961 @@
+// fg_search_warp.cu -- the search with one warp per query.
+//
+// Same search as fg_search.cu (the reference's QuantizedPrunedBeamSearch,
+// SophiaSun18/FlashGANN src/adaptive_search.cuh:5-466, bit for bit), laid out
+// for throughput instead of per-query latency: each warp of a CTA is an
+// independent worker that pulls query ids from the global counter and runs
+// the whole iteration on its own, with no block barrier anywhere.  A CTA
+// holds kWarpsPerCta queries; the per-warp state (beam, visited set, bit
+// planes, candidate buffer) is a private slice of shared memory.
+//
+// Per iteration the warp
+//   * merges the pending candidates into the beam in place: candidate m lands
+//     at pos[m] = m + #{beam <= cand[m]} (the stable, beam-first merge), and
+//     the beam tail is shifted chunk by chunk from the end.  The reference's
+//     merge path differs from the stable merge only where a beam entry and a
+//     candidate have equal distances at one of its segment boundaries; when a
+//     candidate ties the beam the warp computes the reference's split at every
+//     segment boundary first and replays its per-segment merge;
+//   * picks the expanders and runs the adaptive controller (warp-uniform
+//     registers);
+//   * expands: lane l holds neighbour l of every parent (ids, factors and
+//     packed codes loaded for all parents before any is examined), visited
+//     lookups, bit-plane RaBitQ estimates and the keep rule per parent;
+//   * compacts the kept children (first parent wins a shared child) with
+//     __match_any_sync, inserts them into the visited set and computes their
+//     exact distances G rows at a time: every lane accumulates its strided
+//     dimensions of each row in the reference's order, then the reference's
+//     shuffle tree runs transposed (lanes split the rows), which gives the
+//     same sums with G-1+log2(32/G) shuffles instead of 5 per row.
+#include <cfloat>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+
+#include <cuda_runtime.h>
+
+#include "fg_config.h"
+#include "fg_device.cuh"
+#include "fg_internal.h"
+
+static_assert(BUFFER_BOUND <= 32, "the warp kernel keeps at most 32 candidates per iteration");
+static_assert(SEARCH_WIDTH <= 32, "expanders are picked by one warp");
+
+namespace fg {
+namespace {
+
+constexpr int kWarpsPerCta = 4;
+constexpr int kMinCtas = 4;  // 16 warps per SM: 128 registers per thread
+
+struct WPlan {
+    uint32_t padded, cbs, collect_cap;
+    uint32_t slots;  // visited-set slots, a multiple of 32
+    float phase2_rho;
+    int max_iter;
+    int mp_active;
+    uint32_t slice;  // shared-memory bytes per warp
+};
+
+// One warp's slice of the CTA's dynamic shared memory.
+struct WSlice {
+    uint32_t* bidx;
+    float* bdist;
+    uint32_t* hash;
+    uint32_t* planes;
+    uint32_t* wrap;
+    uint32_t* cidx;   // candidate buffer (32 entries)
+    float* cdist;
+    uint32_t* stage;  // kept children in (parent, rank) order, or the evaluation list
+    uint32_t* eslot;  // single-expander path: candidate slot of each evaluation
+    uint32_t* pos;    // merge path with ties: stable positions of the candidates
+    uint32_t* pnode;  // expanders of the iteration
+    float* pdist;
+    uint16_t* split;  // merge path with ties: the reference's split at each segment boundary
+    QueryState* qs;
+};
+
+__host__ __device__ inline size_t a16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
+
+__host__ __device__ inline size_t slice_layout(uint32_t padded, uint32_t slots, int D, bool mp, WSlice* s,
+                                               unsigned char* base) {
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        unsigned char* p = base ? base + off : nullptr;
+        off += a16(bytes);
+        return p;
+    };
+    const int W = D / 32;
+    unsigned char* p;
+    p = take(static_cast<size_t>(slots) * 4); if (s) s->hash = reinterpret_cast<uint32_t*>(p);
+    p = take(padded * 4); if (s) s->bidx = reinterpret_cast<uint32_t*>(p);
+    p = take(padded * 4); if (s) s->bdist = reinterpret_cast<float*>(p);
+    p = take(static_cast<size_t>(kPlanes) * W * 4); if (s) s->planes = reinterpret_cast<uint32_t*>(p);
+    p = take(static_cast<size_t>(W) * 4); if (s) s->wrap = reinterpret_cast<uint32_t*>(p);
+    p = take(32 * 4); if (s) s->cidx = reinterpret_cast<uint32_t*>(p);
+    p = take(32 * 4); if (s) s->cdist = reinterpret_cast<float*>(p);
+    p = take(32 * 4); if (s) s->stage = reinterpret_cast<uint32_t*>(p);
+    p = take(32 * 4); if (s) s->eslot = reinterpret_cast<uint32_t*>(p);
+    p = take(32 * 4); if (s) s->pos = reinterpret_cast<uint32_t*>(p);
+    p = take(SEARCH_WIDTH * 4); if (s) s->pnode = reinterpret_cast<uint32_t*>(p);
+    p = take(SEARCH_WIDTH * 4); if (s) s->pdist = reinterpret_cast<float*>(p);
+    p = take(mp ? (BLOCK_SIZE + 1) * 2 : 0); if (s) s->split = reinterpret_cast<uint16_t*>(p);
+    p = take(sizeof(QueryState)); if (s) s->qs = reinterpret_cast<QueryState*>(p);
+    return off;
+}
+
+// ---------------------------------------------------------------- visited set
+// Exact set as in fg_device.cuh (buckets of 4 slots, linear probing, one
+// 128-bit load per bucket), over any multiple of 4 slots: the bucket is the
+// high word of (Fibonacci hash x bucket count).
+__device__ __forceinline__ uint32_t w_bucket(uint32_t key, uint32_t slots) {
+    return __umulhi(key * 0x9E3779B1u, slots >> 2) << 2;
+}
+
+__device__ __forceinline__ bool w_insert(uint32_t* t, uint32_t slots, uint32_t key) {
+    uint32_t b = w_bucket(key, slots);
+    for (uint32_t n = 0; n < slots; n += 4) {
+        const uint4 v = *reinterpret_cast<const uint4*>(t + b);
+        const uint32_t sl[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (sl[j] == key) return false;
+            if (sl[j] == kMax) {
+                const uint32_t old = atomicCAS(&t[b + j], kMax, key);
+                if (old == kMax) return true;
+                if (old == key) return false;
+            }
+        }
+        b += 4;
+        if (b >= slots) b = 0;
+    }
+    return false;
+}
+
+__device__ __noinline__ bool w_contains_probe(const uint32_t* t, uint32_t slots, uint32_t key, uint32_t b) {
+    for (uint32_t n = 4; n < slots; n += 4) {
+        b += 4;
+        if (b >= slots) b = 0;
+        const uint4 v = *reinterpret_cast<const uint4*>(t + b);
+        if (v.x == key || v.y == key || v.z == key || v.w == key) return true;
+        if (v.x == kMax || v.y == kMax || v.z == kMax || v.w == kMax) return false;
+    }
+    return false;
+}
+
+// first bucket inline; a full bucket without the key continues out of line
+__device__ __forceinline__ bool w_contains(const uint32_t* t, uint32_t slots, uint32_t key) {
+    const uint32_t b = w_bucket(key, slots);
+    const uint4 v = *reinterpret_cast<const uint4*>(t + b);
+    if (v.x == key || v.y == key || v.z == key || v.w == key) return true;
+    if (v.x == kMax || v.y == kMax || v.z == kMax || v.w == kMax) return false;
+    return w_contains_probe(t, slots, key, b);
+}
+
+__device__ __forceinline__ void w_clear(uint32_t* t, uint32_t slots, int lane) {
+    const uint4 e = make_uint4(kMax, kMax, kMax, kMax);
+    for (uint32_t i = static_cast<uint32_t>(lane) * 4; i < slots; i += 128) *reinterpret_cast<uint4*>(t + i) = e;
+}
+
+// ------------------------------------------------------------ exact distances
+// Distance of one row, query dimensions lane, lane+32, ... in registers:
+// the reference's lane-strided fused accumulation and shfl_down tree
+// (include/utils.cuh:270-305).
+template <int W>
+__device__ __forceinline__ float dist_one(const float* __restrict__ r, const float (&q)[W], int dim, int use_ip,
+                                          int lane) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+        const int d = lane + 32 * k;
+        if (d < dim) {
+            const float x = __ldg(r + d);
+            if (use_ip) {
+                acc = __fmaf_rn(q[k], x, acc);
+            } else {
+                const float df = __fsub_rn(q[k], x);
+                acc = __fmaf_rn(df, df, acc);
+            }
+        }
+    }
+    const float s = tree_sum(acc);
+    return use_ip ? -s : s;
+}
+
+// Exact distances of G rows nd[0..G) (the last rows of a short round repeat
+// a valid row and are not written).  Lane l accumulates dimensions l, l+32,
+// ... of every row (every load is issued before the first multiply-add; a
+// dimension >= dim adds fma(0, 0, acc) = acc); then the reference's shuffle
+// tree runs transposed: the level with offset o adds the partial of virtual
+// lane v+o to that of v, and while a lane still holds several rows it keeps
+// half of them and trades the other half with lane l^o.  Every sum is formed
+// from the same two operands as in the reference's tree.
+template <int W, int G>
+__device__ __forceinline__ void eval_round(const float* __restrict__ rows, uint64_t rowf, int dim, const float (&q)[W],
+                                           int use_ip, const uint32_t (&nd)[G], int valid, float* out,
+                                           const uint32_t* slot, int e0, int lane) {
+    constexpr int LG = G == 32 ? 5 : G == 16 ? 4 : G == 8 ? 3 : G == 4 ? 2 : G == 2 ? 1 : 0;
+    static_assert((1 << LG) == G, "G must be a power of two <= 32");
+    float x[G][W];
+#pragma unroll
+    for (int r = 0; r < G; ++r) {
+        const float* p = rows + static_cast<uint64_t>(nd[r]) * rowf + lane;
+#pragma unroll
+        for (int k = 0; k < W; ++k) x[r][k] = (lane + 32 * k < dim) ? __ldg(p + 32 * k) : 0.0f;
+    }
+    float acc[G];
+#pragma unroll
+    for (int r = 0; r < G; ++r) {
+        acc[r] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < W; ++k) {
+            const float df = __fsub_rn(q[k], x[r][k]);
+            acc[r] = use_ip ? __fmaf_rn(q[k], x[r][k], acc[r]) : __fmaf_rn(df, df, acc[r]);
+        }
+    }
+#pragma unroll
+    for (int lvl = 0; lvl < 5; ++lvl) {
+        const int o = 16 >> lvl;
+        const int nr = G >> lvl;
+        if (nr > 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < nr / 2; ++i) {
+                const float send = up ? acc[i] : acc[i + nr / 2];
+                const float keep = up ? acc[i + nr / 2] : acc[i];
+                acc[i] = __fadd_rn(keep, __shfl_xor_sync(kFull, send, o));
+            }
+        } else {
+            acc[0] = __fadd_rn(acc[0], __shfl_xor_sync(kFull, acc[0], o));
+        }
+    }
+    const int r = lane >> (5 - LG);
+    if ((lane & ((1 << (5 - LG)) - 1)) == 0 && r < valid) {
+        const int e = e0 + r;
+        out[slot ? slot[e] : e] = use_ip ? -acc[0] : acc[0];
+    }
+}
+
+// Exact distances of nodes[0..n) into out[slot ? slot[e] : e]: rounds of
+// GB rows, and one round of GB/2 rows for a remainder that fits it.
+template <int W, int GB>
+__device__ __forceinline__ void eval_nodes(const float* __restrict__ rows, uint64_t rowf, int dim, const float (&q)[W],
+                                           int use_ip, const uint32_t* nodes, int n, float* out, const uint32_t* slot,
+                                           int lane) {
+    int e0 = 0;
+    for (; n - e0 > GB / 2; e0 += GB) {
+        uint32_t nd[GB];
+#pragma unroll
+        for (int r = 0; r < GB; ++r) nd[r] = nodes[e0 + r < n ? e0 + r : n - 1];
+        eval_round<W, GB>(rows, rowf, dim, q, use_ip, nd, n - e0, out, slot, e0, lane);
+    }
+    if (e0 < n) {
+        uint32_t nd[GB / 2];
+#pragma unroll
+        for (int r = 0; r < GB / 2; ++r) nd[r] = nodes[e0 + r < n ? e0 + r : n - 1];
+        eval_round<W, GB / 2>(rows, rowf, dim, q, use_ip, nd, n - e0, out, slot, e0, lane);
+    }
+}
+
+// L2 prefetch of a row's raw vector (128-byte lines).
+__device__ __forceinline__ void prefetch_row(const float* r, int dim) {
+    for (int l = 0; l < dim; l += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(r + l));
+}
+
+// ------------------------------------------------------------ merge path
+// Merge of the candidate buffer (cidx/cdist[0..cbs)) into the beam
+// (bidx/bdist[0..P)) with the reference's merge-path result
+// (include/utils.cuh:618-680): sorts the candidates with the 32-lane network
+// and returns p0 = #{beam < cand[0]}, the first position that can change.
+// Stable (beam-first) merge in place: output o >= p0 is candidate m if
+// pos[m] == o, else beam[o - #{pos < o}].  Chunks of 32 positions are
+// rewritten from the end, four per step (all reads of a step before its
+// writes; every source index is <= its output, so lower chunks are intact).
+__device__ __forceinline__ void stable_shift(uint32_t* bidx, float* bdist, float k, uint32_t v, uint32_t pos, uint32_t P,
+                                             uint32_t p0, int lane) {
+    const int first = static_cast<int>(p0 & ~31u);
+    for (int g = static_cast<int>((P - 1) & ~31u); g >= first; g -= 128) {
+        float od[4];
+        uint32_t ov[4];
+        bool act[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int c0 = g - 32 * u;
+            act[u] = false;
+            od[u] = 0.0f;
+            ov[u] = 0;
+            if (c0 >= first) {
+                const uint32_t uc0 = static_cast<uint32_t>(c0);
+                const uint32_t below = __popc(__ballot_sync(kFull, pos < uc0));
+                const uint32_t rel = pos - uc0;
+                const uint32_t hit = __reduce_or_sync(kFull, (pos >= uc0 && rel < 32u) ? (1u << rel) : 0u);
+                const uint32_t o = uc0 + lane;
+                const uint32_t cnt = below + __popc(hit & lanemask_lt(lane));
+                const float ck = __shfl_sync(kFull, k, cnt & 31u);
+                const uint32_t cv = __shfl_sync(kFull, v, cnt & 31u);
+                act[u] = o < P && o >= p0;
+                if (act[u]) {
+                    if ((hit >> lane) & 1u) {
+                        od[u] = ck;
+                        ov[u] = cv;
+                    } else {
+                        od[u] = bdist[o - cnt];
+                        ov[u] = bidx[o - cnt];
+                    }
+                }
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (act[u]) {
+                const uint32_t o = static_cast<uint32_t>(g - 32 * u) + lane;
+                bdist[o] = od[u];
+                bidx[o] = ov[u];
+            }
+        }
+        __syncwarp();
+    }
+}
+
+// Fix-up storage inside the slice's split area (the full replay, which uses
+// split[], only runs when the fix-ups do not fit).
+constexpr int kMaxFixSegments = 8;
+struct FixArea {
+    uint32_t* mask;  // segment flags, (BLOCK_SIZE + 32) / 32 words
+    uint32_t* list;  // flagged segment ids
+    uint32_t* idx;   // 4 * kMaxFixSegments outputs
+    float* dist;
+    uint16_t* at;    // output position, 0xFFFF = unused
+};
+__device__ __forceinline__ FixArea fix_area(const WSlice& s) {
+    unsigned char* b = reinterpret_cast<unsigned char*>(s.split);
+    FixArea f;
+    f.mask = reinterpret_cast<uint32_t*>(b);
+    f.list = reinterpret_cast<uint32_t*>(b + 64);
+    f.idx = reinterpret_cast<uint32_t*>(b + 128);
+    f.dist = reinterpret_cast<float*>(b + 128 + 4 * 4 * kMaxFixSegments);
+    f.at = reinterpret_cast<uint16_t*>(b + 128 + 8 * 4 * kMaxFixSegments);
+    return f;
+}
+static_assert((BLOCK_SIZE + 32) / 32 <= 16 && kMaxFixSegments <= 16, "flags and ids fit in 64 bytes each");
+static_assert(128 + 10 * 4 * kMaxFixSegments <= (BLOCK_SIZE + 1) * 2, "fix-ups fit in the split area");
+
+__device__ __noinline__ int tie_fixups(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+                                       uint32_t p0, uint32_t lb, uint32_t ub, bool tie, int lane);
+__device__ __noinline__ void merge_path_ties(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+                                             uint32_t p0, int lane);
+
+// Merge of the candidate buffer (cidx/cdist[0..cbs)) into the beam
+// (bidx/bdist[0..P)) with the reference's merge-path result
+// (include/utils.cuh:618-680): sorts the candidates with the 32-lane network
+// and returns p0 = #{beam < cand[0]}, the first position that can change.
+// The merge path equals the stable merge except at a segment boundary where a
+// beam entry and a candidate tie: those segments are replayed with the
+// reference's splits before the stable shift and written over it.
+__device__ uint32_t merge_path_warp(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+                                    int lane) {
+    uint32_t* bidx = s.bidx;
+    float* bdist = s.bdist;
+    const bool valid = lane < static_cast<int>(cbs);
+    float k = valid ? s.cdist[lane] : FLT_MAX;
+    uint32_t v = valid ? s.cidx[lane] : kMax;
+    sort32(k, v, lane);
+    __syncwarp();
+    if (valid) {
+        s.cdist[lane] = k;
+        s.cidx[lane] = v;
+    }
+    const uint32_t lb = lower_bound(bdist, P, k);
+    uint32_t ub = lb;
+    if (k == FLT_MAX) ub = P;
+    else if (lb < P && bdist[lb] == k) ub = upper_bound(bdist, P, k);
+    const uint32_t pos = valid ? static_cast<uint32_t>(lane) + ub : kMax;
+    const uint32_t p0 = __shfl_sync(kFull, lb, 0);
+    const bool tie = valid && k != FLT_MAX && lb < ub;
+    __syncwarp();
+    // nothing enters the beam: no candidate before position P, and none ties
+    // the beam (a tie at diagonal P can swap the last entry for a candidate)
+    if (__ballot_sync(kFull, pos < P || tie) == 0) return p0;
+    int nfix = 0;
+    if (__ballot_sync(kFull, tie) != 0) {
+        if (valid) s.pos[lane] = pos;
+        __syncwarp();
+        nfix = tie_fixups(s, cbs, P, active, bnd, p0, lb, ub, tie, lane);
+        if (nfix < 0) {
+            merge_path_ties(s, cbs, P, active, bnd, p0, lane);
+            return p0;
+        }
+    }
+    stable_shift(bidx, bdist, k, v, pos, P, p0, lane);
+    if (nfix > 0) {
+        const FixArea f = fix_area(s);
+        if (lane < 4 * nfix && f.at[lane] != 0xFFFFu) {
+            bidx[f.at[lane]] = f.idx[lane];
+            bdist[f.at[lane]] = f.dist[lane];
+        }
+        __syncwarp();
+    }
+    return p0;
+}
+
+__device__ __forceinline__ int count_lt(const uint32_t* a, int n, uint32_t x) {
+    int lo = 0, hi = n;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (a[mid] < x) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// Flags the segments next to a boundary whose reference split differs from
+// the stable one (only diagonals lb+m+1 .. ub+m of a tied candidate m can),
+// and replays each flagged segment with the reference's splits into the
+// fix-up list.  Returns the number of flagged segments, or -1 if they do not
+// fit the list.
+__device__ __noinline__ int tie_fixups(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+                                       uint32_t p0, uint32_t lb, uint32_t ub, bool tie, int lane) {
+    if (P > 4u * static_cast<uint32_t>(active)) return -1;  // segments longer than the list's 4 outputs
+    const FixArea f = fix_area(s);
+    constexpr int kWords = (BLOCK_SIZE + 32) / 32;
+    if (lane < kWords) f.mask[lane] = 0;
+    __syncwarp();
+    if (tie) {
+        const uint32_t lo0 = lb + lane + 1, hi0 = ub + lane;
+        const uint32_t lo = lo0 > p0 + 1 ? lo0 : p0 + 1;
+        const uint32_t hi = hi0 < P ? hi0 : P;
+        if (lo <= hi) {
+            for (uint32_t sg = (lo * static_cast<uint32_t>(active) + P - 1) / P;
+                 sg <= static_cast<uint32_t>(active) && bnd[sg] <= hi; ++sg) {
+                const int d = bnd[sg];
+                const int stable = d - count_lt(s.pos, static_cast<int>(cbs), static_cast<uint32_t>(d));
+                const int ref = split_at(d, p0, s.pos, s.bdist, static_cast<int>(P), s.cdist, static_cast<int>(cbs));
+                if (ref != stable) {
+                    atomicOr(&f.mask[(sg - 1) >> 5], 1u << ((sg - 1) & 31));
+                    if (sg < static_cast<uint32_t>(active)) atomicOr(&f.mask[sg >> 5], 1u << (sg & 31));
+                }
+            }
+        }
+    }
+    __syncwarp();
+    const uint32_t w = lane < kWords ? f.mask[lane] : 0u;
+    uint32_t incl = __popc(w);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const int total = static_cast<int>(__shfl_sync(kFull, incl, 31));
+    if (total == 0 || total > kMaxFixSegments) return total == 0 ? 0 : -1;
+    // segment ids in flag order, one per lane (j < total)
+    __syncwarp();
+    uint32_t* list = f.list;
+    {
+        uint32_t m = w, at = incl - __popc(w);
+        while (m) {
+            const int b = __ffs(m) - 1;
+            m &= m - 1;
+            list[at++] = static_cast<uint32_t>(lane * 32 + b);
+        }
+    }
+    __syncwarp();
+    if (lane < 4 * total) f.at[lane] = 0xFFFFu;
+    __syncwarp();
+    if (lane < total) {
+        const int sg = static_cast<int>(list[lane]);
+        const int ob = bnd[sg], oe = bnd[sg + 1];
+        int ti = split_at(ob, p0, s.pos, s.bdist, static_cast<int>(P), s.cdist, static_cast<int>(cbs));
+        const int te = split_at(oe, p0, s.pos, s.bdist, static_cast<int>(P), s.cdist, static_cast<int>(cbs));
+        int ci = ob - ti;
+        const int ce = oe - te;
+        for (int o = ob; o < oe; ++o) {
+            const int e = 4 * lane + (o - ob);
+            const bool take = (ci >= ce) || (ti < te && s.bdist[ti] <= s.cdist[ci]);
+            f.at[e] = static_cast<uint16_t>(o);
+            if (take) {
+                f.idx[e] = s.bidx[ti];
+                f.dist[e] = s.bdist[ti];
+                ++ti;
+            } else {
+                f.idx[e] = s.cidx[ci];
+                f.dist[e] = s.cdist[ci];
+                ++ci;
+            }
+        }
+    }
+    __syncwarp();
+    return total;
+}
+
+// A candidate ties a beam entry: the reference's split at every segment
+// boundary (split_at runs its binary search where the split is ambiguous),
+// computed before the beam is overwritten, then each output position replays
+// its segment's beam-first merge; positions are rewritten from the end and
+// every source index is <= its output.
+__device__ __noinline__ void merge_path_ties(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+                                             uint32_t p0, int lane) {
+    uint32_t* bidx = s.bidx;
+    float* bdist = s.bdist;
+    const uint32_t first_chunk = p0 & ~31u;
+    for (int s0 = 0; s0 <= active; s0 += 32) {
+        const int sg = s0 + lane;
+        if (sg <= active) {
+            const int d = bnd[sg];
+            s.split[sg] = static_cast<uint16_t>(
+                d <= static_cast<int>(p0) ? d
+                                          : split_at(d, p0, s.pos, bdist, static_cast<int>(P), s.cdist, static_cast<int>(cbs)));
+        }
+    }
+    __syncwarp();
+    for (int c0 = static_cast<int>((P - 1) & ~31u); c0 >= static_cast<int>(first_chunk); c0 -= 32) {
+        const uint32_t o = static_cast<uint32_t>(c0) + lane;
+        const bool act = o < P && o >= p0;
+        float od = 0.0f;
+        uint32_t ov = 0;
+        if (act) {
+            uint32_t sg = (o * static_cast<uint32_t>(active)) / P;  // o * active < 2^18
+            if (bnd[sg + 1] <= o) ++sg;
+            const int ob = bnd[sg], oe = bnd[sg + 1];
+            int ti = s.split[sg];
+            const int te = s.split[sg + 1];
+            int ci = ob - ti;
+            const int ce = oe - te;
+            for (int j = ob;; ++j) {
+                const bool take = (ci >= ce) || (ti < te && bdist[ti] <= s.cdist[ci]);
+                if (j == static_cast<int>(o)) {
+                    if (take) {
+                        od = bdist[ti];
+                        ov = bidx[ti];
+                    } else {
+                        od = s.cdist[ci];
+                        ov = s.cidx[ci];
+                    }
+                    break;
+                }
+                if (take) ++ti;
+                else ++ci;
+            }
+        }
+        __syncwarp();
+        if (act) {
+            bdist[o] = od;
+            bidx[o] = ov;
+        }
+        __syncwarp();
+    }
+}
+
+// -------------------------------------------------------------- the search
+// Visited-set reset to the beam's nodes (src/adaptive_search.cuh:129-133).
+__device__ __noinline__ void restore_visited(const WSlice& s, uint32_t slots, int beam, int lane) {
+    w_clear(s.hash, slots, lane);
+    __syncwarp();
+    for (int i = lane; i < beam; i += 32) w_insert(s.hash, slots, s.bidx[i] & ~kMsb);
+    __syncwarp();
+}
+
+template <int W, int MERGE>
+__device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& pl, const WSlice& s,
+                                             const uint16_t* bnd, uint32_t qid, bool vec, int lane) {
+    constexpr bool mp = MERGE == 0;
+    constexpr int G = W <= 4 ? 16 : 8;  // rows per exact-distance round
+    const int dim = a.dim, deg = a.degree, beam = a.beam;
+    const uint32_t P = pl.padded, cbs = pl.cbs, slots = pl.slots;
+    const float* __restrict__ rows = a.rows;
+    const uint64_t rowf = a.row;
+    uint32_t* bidx = s.bidx;
+    float* bdist = s.bdist;
+
+    // ---------------------------------------------------------------- init
+    const float* q = a.queries + static_cast<size_t>(qid) * dim;
+    float qr[W];
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+        const int d = lane + 32 * k;
+        qr[k] = d < dim ? __ldg(q + d) : 0.0f;
+    }
+    {
+        // rotation + quantisation, with the visited table as scratch
+        float* qv = reinterpret_cast<float*>(s.hash);
+        uint8_t* quant = reinterpret_cast<uint8_t*>(qv + ((dim + 3) & ~3));
+        for (int i = lane; i < dim; i += 32) qv[i] = q[i];
+        __syncwarp();
+        prep_warp<W>(qv, a.signs, dim, quant, nullptr, s.qs, lane);
+        build_planes(quant, 32 * W, s.planes, s.wrap, s.qs, lane);
+        __syncwarp();
+    }
+    const QueryState qsl = *s.qs;
+    __syncwarp();
+    w_clear(s.hash, slots, lane);
+    for (uint32_t i = lane; i < P; i += 32) {
+        bidx[i] = kMax;
+        bdist[i] = FLT_MAX;
+    }
+    s.cidx[lane] = kMax;
+    s.cdist[lane] = FLT_MAX;
+    __syncwarp();
+    // entry point into candidate slot 0 (src/adaptive_search.cuh:110-118)
+    const float ed = dist_one<W>(rows + static_cast<uint64_t>(a.entry) * rowf, qr, dim, a.use_ip, lane);
+    if (lane == 0) {
+        s.cidx[0] = a.entry;
+        s.cdist[0] = ed;
+        w_insert(s.hash, slots, a.entry);
+    }
+    __syncwarp();
+    CtlRegs c;
+    c.theta = PHASE1_THETA;
+    c.rho = PHASE1_RHO;
+    c.policy_iters = 0;
+    c.top1 = kMax;
+    c.stall = 0;
+    c.warmup_done = false;
+    c.entry_d = ed;
+    c.last_d = FLT_MAX;
+    c.cur_d = FLT_MAX;
+    c.scan = 0;
+    uint32_t c_iters = 0, c_exp = 0, c_eval = 1, n_est = 0;
+
+    // ---------------------------------------------------------------- loop
+    for (int iter = 0; iter < MAX_ITERATIONS; ++iter) {
+        if ((iter + 1) % SMALL_HASH_RESET_INTERVAL == 0) restore_visited(s, slots, beam, lane);
+        if (iter >= pl.max_iter) break;
+
+        // merge the previous iteration's candidates (:142-145)
+        uint32_t p0 = 0;
+        if constexpr (mp) {
+            p0 = merge_path_warp(s, cbs, P, pl.mp_active, bnd, lane);
+        } else {
+            merge_bitonic<MERGE>(bidx, bdist, s.cidx, s.cdist, cbs, iter == 0, lane);
+            for (uint32_t i = static_cast<uint32_t>(beam) + lane; i < P; i += 32) {
+                bidx[i] = kMax;
+                bdist[i] = FLT_MAX;
+            }
+            __syncwarp();
+        }
+        ++c_iters;
+
+        // control (src/adaptive_search.cuh:147-217)
+        const float cutoff = bidx[beam - 1] == kMax ? FLT_MAX : bdist[(a.K < beam ? a.K : beam) - 1];
+        const uint32_t b0 = bidx[0];
+        __syncwarp();
+        s.cidx[lane] = kMax;
+        s.cdist[lane] = FLT_MAX;
+        controller_update(c, b0, iter, pl.phase2_rho);
+        uint32_t start = 0;
+        if constexpr (mp) {
+            if (p0 < c.scan) c.scan = p0;
+            start = c.scan & ~31u;
+        }
+        // pick_expanders (include/utils.cuh:752-787)
+        const uint32_t theta = static_cast<uint32_t>(c.theta);
+        uint32_t num = 0, last_pick = 0;
+        const uint32_t lim = (static_cast<uint32_t>(beam) + 31u) & ~31u;
+        for (uint32_t j0 = start; j0 < lim; j0 += 32) {
+            const uint32_t j = j0 + lane;
+            uint32_t e = 0;
+            const bool np = j < static_cast<uint32_t>(beam) && ((e = bidx[j]) & kMsb) == 0;
+            const uint32_t b = __ballot_sync(kFull, np);
+            const uint32_t i = __popc(b & lanemask_lt(lane)) + num;
+            if (np && i < theta) {
+                s.pnode[i] = e & 0x7fffffffu;
+                s.pdist[i] = bdist[j];
+                bidx[j] = e | kMsb;
+            }
+            if (num + __popc(b) >= theta) {
+                const uint32_t sel = __ballot_sync(kFull, np && i == theta - 1);
+                last_pick = j0 + (__ffs(sel) - 1);
+                num = theta;
+                // prefetch the blocks of the next unexpanded entries of this chunk
+                const uint32_t later = b & ~((sel << 1) - 1u);
+                if ((later >> lane) & 1u) {
+                    const char* blk = reinterpret_cast<const char*>(rows + static_cast<uint64_t>(e & 0x7fffffffu) * rowf +
+                                                                    a.code_off);
+#pragma unroll
+                    for (int l = 0; l < 8; ++l) asm volatile("prefetch.global.L2 [%0];" ::"l"(blk + 128 * l));
+                }
+                break;
+            }
+            num += __popc(b);
+        }
+        __syncwarp();
+        if constexpr (mp) c.scan = num == theta ? last_pick + 1 : static_cast<uint32_t>(beam);
+        if (num) {
+            // record_selected_expander_dist (adaptive_search_utils.cuh:41-49)
+            c.last_d = finite_lt_max(c.cur_d) ? c.cur_d : c.entry_d;
+            c.cur_d = s.pdist[num - 1];
+        }
+        if (a.trace && iter < a.trace_cap) {
+            const size_t base = static_cast<size_t>(qid) * a.trace_cap + iter;
+            if (lane < SEARCH_WIDTH) a.trace[base * SEARCH_WIDTH + lane] = lane < static_cast<int>(num) ? s.pnode[lane] : kMax;
+            if (lane == 0) a.trace_count[base] = static_cast<int32_t>(num);
+        }
+        if (!num) break;
+        c_exp += num;
+        const int th = c.theta;
+        const float rho = c.rho;
+        const bool cut_ok = isfinite(cutoff) && cutoff < FLT_MAX;
+
+        if (!(th > 1)) {
+            // ---------------------------- single expander (src/adaptive_search.cuh:221-343)
+            const uint32_t work = static_cast<uint32_t>(deg) < cbs ? static_cast<uint32_t>(deg) : cbs;
+            const float* prow = rows + static_cast<uint64_t>(s.pnode[0]) * rowf;
+            const float pd = s.pdist[0];
+            ParentLane<W> p;
+            load_parent<W>(prow, a, static_cast<int>(work), vec, lane, p);
+            const bool in_work = static_cast<uint32_t>(lane) < work;
+            uint32_t child = p.child;
+            if (child != kMax && (child >= a.n || w_contains(s.hash, slots, child))) child = kMax;
+            float dist = child == kMax ? FLT_MAX : 0.0f;
+            const int keep = keep_for(work, th, rho, false, 0);
+            const uint32_t vcount = __popc(__ballot_sync(kFull, in_work && child != kMax));
+            int admit = static_cast<int>(work);
+            if (keep < static_cast<int>(vcount)) {
+                if (child != kMax) {
+                    // theta = 1 variant: triple_x == FLT_MAX estimates 0.0 (include/utils.cuh:951-952)
+                    float est = 0.0f;
+                    if (p.tx != FLT_MAX) {
+                        const uint32_t raw = parent_raw<W>(p, prow, a, lane, s.planes, s.wrap, qsl.wrap_any);
+                        est = estimate(raw, p.tx, p.fdq, p.fvq, pd, qsl);
+                    }
+                    if (isfinite(est)) {
+                        dist = est;
+                    } else {
+                        dist = FLT_MAX;
+                        child = kMax;
+                    }
+                }
+                n_est += vcount;
+                const uint32_t near =
+                    cut_ok ? __popc(__ballot_sync(kFull, in_work && child != kMax && isfinite(dist) && dist <= cutoff)) : 0u;
+                const int eff = keep_for(work, th, rho, cut_ok, near);
+                float kk = lane < static_cast<int>(cbs) ? dist : FLT_MAX;
+                uint32_t vv = lane < static_cast<int>(cbs) ? child : kMax;
+                sort32(kk, vv, lane);
+                if (lane >= eff) {
+                    kk = FLT_MAX;
+                    vv = kMax;
+                }
+                dist = kk;
+                child = vv;
+                admit = eff;
+            }
+            // insert kept children (first occurrence wins), list them for evaluation
+            const bool want = lane < admit && child != kMax && dist < FLT_MAX;
+            const uint32_t same = __match_any_sync(kFull, want ? child : kMax);
+            const bool first = want && (__ffs(same) - 1) == lane;
+            const bool ins = first && w_insert(s.hash, slots, child);
+            if (lane < static_cast<int>(cbs)) s.cidx[lane] = ins ? child : kMax;
+            const uint32_t ib = __ballot_sync(kFull, ins);
+            if (ins) {
+                const uint32_t r = __popc(ib & lanemask_lt(lane));
+                s.stage[r] = child;
+                s.eslot[r] = lane;
+                prefetch_row(rows + static_cast<uint64_t>(child) * rowf, dim);
+            }
+            __syncwarp();
+            const int ne = __popc(ib);
+            c_eval += ne;
+            eval_nodes<W, G>(rows, rowf, dim, qr, a.use_ip, s.stage, ne, s.cdist, s.eslot, lane);
+            __syncwarp();
+        } else {
+            // ----------------------- speculative expanders (src/adaptive_search.cuh:344-444)
+            // degree <= 32: lane l holds neighbour l of every parent; every
+            // lookup of the iteration happens before its inserts.
+            const uint32_t active = static_cast<uint32_t>(deg) < 32u ? static_cast<uint32_t>(deg) : 32u;
+            const int keep0 = keep_for(active, th, rho, false, 0);
+            // one parent per step; the next parent's block is loaded while
+            // this one is examined (the last step reloads its own block)
+            ParentLane<W> cur;
+            load_parent<W>(rows + static_cast<uint64_t>(s.pnode[0]) * rowf, a, deg, vec, lane, cur);
+            uint32_t total = 0;
+#pragma unroll 1
+            for (int t = 0; t < static_cast<int>(num); ++t) {
+                const int tn = t + 1 < static_cast<int>(num) ? t + 1 : t;
+                ParentLane<W> nxt;
+                load_parent<W>(rows + static_cast<uint64_t>(s.pnode[tn]) * rowf, a, deg, vec, lane, nxt);
+                const uint32_t child = cur.child;
+                bool valid = child != kMax && child < a.n && !w_contains(s.hash, slots, child);
+                const uint32_t raw_valid = __popc(__ballot_sync(kFull, valid));
+                bool kl;
+                if (keep0 >= static_cast<int>(raw_valid)) {
+                    kl = valid;
+                } else {
+                    float est = FLT_MAX;
+                    if (valid) {
+                        // speculative variant: triple_x == FLT_MAX estimates FLT_MAX
+                        if (cur.tx != FLT_MAX) {
+                            const float* prow = rows + static_cast<uint64_t>(s.pnode[t]) * rowf;
+                            const uint32_t raw = parent_raw<W>(cur, prow, a, lane, s.planes, s.wrap, qsl.wrap_any);
+                            est = estimate(raw, cur.tx, cur.fdq, cur.fvq, s.pdist[t], qsl);
+                        }
+                        valid = isfinite(est);
+                    }
+                    n_est += raw_valid;
+                    const uint32_t near = __popc(__ballot_sync(kFull, valid && cut_ok && est <= cutoff));
+                    const int eff = keep_for(active, th, rho, cut_ok, near);
+                    kl = keep_smallest(est, valid, eff, lane);
+                }
+                const uint32_t kb = __ballot_sync(kFull, kl);
+                if (kl) {
+                    const uint32_t r = total + __popc(kb & lanemask_lt(lane));
+                    if (r < 32u) s.stage[r] = child;
+                    prefetch_row(rows + static_cast<uint64_t>(child) * rowf, dim);
+                }
+                total += __popc(kb);
+                cur = nxt;
+            }
+            __syncwarp();
+            // inserts and compaction in (parent, rank) order; a child kept by
+            // two parents goes to the first (include/utils.cuh:187-214)
+            const uint32_t child = lane < static_cast<int>(total) ? s.stage[lane] : kMax;
+            const uint32_t same = __match_any_sync(kFull, child);
+            const bool first = child != kMax && (__ffs(same) - 1) == lane;
+            const bool ins = first && w_insert(s.hash, slots, child);
+            const uint32_t ib = __ballot_sync(kFull, ins);
+            const uint32_t slot = __popc(ib & lanemask_lt(lane));
+            const uint32_t compact = __popc(ib);
+            const uint32_t ne = compact < pl.collect_cap ? compact : pl.collect_cap;
+            if (ins && slot < pl.collect_cap) s.cidx[slot] = child;
+            __syncwarp();
+            c_eval += ne;
+            eval_nodes<W, G>(rows, rowf, dim, qr, a.use_ip, s.cidx, static_cast<int>(ne), s.cdist, nullptr, lane);
+            __syncwarp();
+        }
+    }
+    // final merge (src/adaptive_search.cuh:448-452)
+    if constexpr (mp) {
+        merge_path_warp(s, cbs, P, pl.mp_active, bnd, lane);
+    } else {
+        merge_bitonic<MERGE>(bidx, bdist, s.cidx, s.cdist, cbs, false, lane);
+    }
+    __syncwarp();
+    // results (:455-464): position i < beam holds the beam entry with its MSB
+    // cleared; positions >= beam repeat the last one
+    for (int i = lane; i < a.K; i += 32) {
+        const int sp = i < beam ? i : beam - 1;
+        a.out_ids[static_cast<size_t>(qid) * a.K + i] = bidx[sp] & 0x7fffffffu;
+        if (a.out_dists) a.out_dists[static_cast<size_t>(qid) * a.K + i] = bdist[sp];
+    }
+    if (lane == 0 && a.stats) {
+        fg_query_stats st;
+        st.iterations = c_iters;
+        st.expansions = c_exp;
+        st.evaluations = c_eval;
+        st.estimates = n_est;
+        a.stats[qid] = st;
+    }
+    __syncwarp();
+}
+
+template <int W, int MERGE>
+__global__ void __launch_bounds__(kWarpsPerCta * 32, kMinCtas) search_warp_kernel(const SearchArgs a, const WPlan pl,
+                                                                                  int vec_codes) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    // merge-path output segment boundaries s * itopk / active (launch constants)
+    __shared__ uint16_t bnd[MERGE == 0 ? BLOCK_SIZE + 1 : 1];
+    if constexpr (MERGE == 0) {
+        for (int sg = threadIdx.x; sg <= pl.mp_active; sg += kWarpsPerCta * 32)
+            bnd[sg] = static_cast<uint16_t>((static_cast<uint32_t>(sg) * pl.padded) / static_cast<uint32_t>(pl.mp_active));
+    }
+    __syncthreads();  // the only block barrier: the warps are independent from here on
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    WSlice s;
+    slice_layout(pl.padded, pl.slots, 32 * W, MERGE == 0, &s, smem_raw + static_cast<size_t>(warp) * pl.slice);
+    for (;;) {
+        uint32_t qid = 0;
+        if (lane == 0) qid = atomicAdd(a.work_counter, 1u);
+        qid = __shfl_sync(kFull, qid, 0);
+        if (qid >= static_cast<uint32_t>(a.nq)) break;
+        search_query<W, MERGE>(a, pl, s, bnd, qid, vec_codes != 0, lane);
+    }
+}
+
+template <int W>
+const void* pick_merge_w(int merge) {
+    switch (merge) {
+        case 1: return reinterpret_cast<const void*>(search_warp_kernel<W, 1>);
+        case 2: return reinterpret_cast<const void*>(search_warp_kernel<W, 2>);
+        case 4: return reinterpret_cast<const void*>(search_warp_kernel<W, 4>);
+        default: return reinterpret_cast<const void*>(search_warp_kernel<W, 0>);
+    }
+}
+
+const void* warp_kernel_for(int W, int merge) {
+    switch (W) {
+        case 1: return pick_merge_w<1>(merge);
+        case 2: return pick_merge_w<2>(merge);
+        case 4: return pick_merge_w<4>(merge);
+        default: return pick_merge_w<8>(merge);
+    }
+}
+
+}  // namespace
+
+bool warp_kernel_supports(int padded_dim) { return padded_dim >= 32 && padded_dim <= 256; }
+
+int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, size_t errlen) {
+    const int D = a.padded_dim;
+    uint32_t req = p->padded + p->cbs * SMALL_HASH_RESET_INTERVAL;
+    uint32_t slots = (req * 4 + 2) / 3;
+    // the table doubles as the query's scratch during set-up
+    const uint32_t scratch = (static_cast<uint32_t>((a.dim + 3) & ~3) * 4 + static_cast<uint32_t>(D) + 3) / 4;
+    if (slots < scratch) slots = scratch;
+    slots = (slots + 31) & ~31u;
+    p->kernel = 1;
+    p->slots = slots;
+    p->slice_bytes = slice_layout(p->padded, slots, D, p->merge_n2 == 0, nullptr, nullptr);
+    p->smem_bytes = p->slice_bytes * kWarpsPerCta;
+    p->threads = kWarpsPerCta * 32;
+    int sms = 0, max_smem = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    if (e != cudaSuccess) {
+        snprintf(err, errlen, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+        return FG_ERR_CUDA;
+    }
+    if (p->smem_bytes > static_cast<size_t>(max_smem)) {
+        snprintf(err, errlen, "shared memory %zu exceeds the device limit %d", p->smem_bytes, max_smem);
+        return FG_ERR_UNSUPPORTED;
+    }
+    const void* fn = warp_kernel_for(D / 32, p->merge_n2);
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p->smem_bytes));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) {
+        snprintf(err, errlen, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        return FG_ERR_CUDA;
+    }
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, p->threads, p->smem_bytes);
+    if (e != cudaSuccess || per_sm < 1) {
+        snprintf(err, errlen, "occupancy query failed: %s", cudaGetErrorString(e));
+        return FG_ERR_CUDA;
+    }
+    p->blocks_per_sm = per_sm;
+    const int resident = per_sm * sms;
+    const int need = (a.nq + kWarpsPerCta - 1) / kWarpsPerCta;
+    p->grid = need < resident ? need : resident;
+    if (p->grid < 1) p->grid = 1;
+    return FG_OK;
+}
+
+cudaError_t launch_search_warp(const SearchArgs& a, const SearchPlan& p, cudaStream_t stream) {
+    WPlan pl;
+    pl.padded = p.padded;
+    pl.cbs = p.cbs;
+    pl.collect_cap = p.collect_cap;
+    pl.slots = p.slots;
+    pl.phase2_rho = p.phase2_rho;
+    pl.max_iter = p.max_iter;
+    pl.mp_active = p.mp_active;
+    pl.slice = static_cast<uint32_t>(p.slice_bytes);
+    cudaError_t e = cudaMemsetAsync(a.work_counter, 0, sizeof(uint32_t), stream);
+    if (e != cudaSuccess) return e;
+    const void* fn = warp_kernel_for(a.padded_dim / 32, p.merge_n2);
+    SearchArgs args = a;
+    int vec = p.vec_codes;
+    void* params[] = {&args, &pl, &vec};
+    return cudaLaunchKernel(fn, dim3(p.grid), dim3(p.threads), params, p.smem_bytes, stream);
+}
+
+}  // namespace fg
