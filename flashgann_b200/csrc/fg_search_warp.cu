@@ -340,9 +340,11 @@ __device__ __forceinline__ FixArea fix_area(const WSlice& s) {
 static_assert((BLOCK_SIZE + 32) / 32 <= 16 && kMaxFixSegments <= 16, "flags and ids fit in 64 bytes each");
 static_assert(128 + 10 * 4 * kMaxFixSegments <= (BLOCK_SIZE + 1) * 2, "fix-ups fit in the split area");
 
-__device__ __noinline__ int tie_fixups(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+__device__ __noinline__ int tie_fixups(uint32_t* s_bidx, float* s_bdist, uint32_t* s_cidx, float* s_cdist,
+                                       uint32_t* s_pos, uint16_t* s_split, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
                                        uint32_t p0, uint32_t lb, uint32_t ub, bool tie, int lane);
-__device__ __noinline__ void merge_path_ties(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+__device__ __noinline__ void merge_path_ties(uint32_t* s_bidx, float* s_bdist, uint32_t* s_cidx, float* s_cdist,
+                                             uint32_t* s_pos, uint16_t* s_split, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
                                              uint32_t p0, int lane);
 
 // Merge of the candidate buffer (cidx/cdist[0..cbs)) into the beam
@@ -352,7 +354,7 @@ __device__ __noinline__ void merge_path_ties(const WSlice& s, uint32_t cbs, uint
 // The merge path equals the stable merge except at a segment boundary where a
 // beam entry and a candidate tie: those segments are replayed with the
 // reference's splits before the stable shift and written over it.
-__device__ uint32_t merge_path_warp(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+__device__ __forceinline__ uint32_t merge_path_warp(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
                                     int lane) {
     uint32_t* bidx = s.bidx;
     float* bdist = s.bdist;
@@ -380,9 +382,9 @@ __device__ uint32_t merge_path_warp(const WSlice& s, uint32_t cbs, uint32_t P, i
     if (__ballot_sync(kFull, tie) != 0) {
         if (valid) s.pos[lane] = pos;
         __syncwarp();
-        nfix = tie_fixups(s, cbs, P, active, bnd, p0, lb, ub, tie, lane);
+        nfix = tie_fixups(s.bidx, s.bdist, s.cidx, s.cdist, s.pos, s.split, cbs, P, active, bnd, p0, lb, ub, tie, lane);
         if (nfix < 0) {
-            merge_path_ties(s, cbs, P, active, bnd, p0, lane);
+            merge_path_ties(s.bidx, s.bdist, s.cidx, s.cdist, s.pos, s.split, cbs, P, active, bnd, p0, lane);
             return p0;
         }
     }
@@ -413,8 +415,16 @@ __device__ __forceinline__ int count_lt(const uint32_t* a, int n, uint32_t x) {
 // and replays each flagged segment with the reference's splits into the
 // fix-up list.  Returns the number of flagged segments, or -1 if they do not
 // fit the list.
-__device__ __noinline__ int tie_fixups(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+__device__ __noinline__ int tie_fixups(uint32_t* s_bidx, float* s_bdist, uint32_t* s_cidx, float* s_cdist,
+                                       uint32_t* s_pos, uint16_t* s_split, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
                                        uint32_t p0, uint32_t lb, uint32_t ub, bool tie, int lane) {
+    WSlice s;
+    s.bidx = s_bidx;
+    s.bdist = s_bdist;
+    s.cidx = s_cidx;
+    s.cdist = s_cdist;
+    s.pos = s_pos;
+    s.split = s_split;
     if (P > 4u * static_cast<uint32_t>(active)) return -1;  // segments longer than the list's 4 outputs
     const FixArea f = fix_area(s);
     constexpr int kWords = (BLOCK_SIZE + 32) / 32;
@@ -492,8 +502,16 @@ __device__ __noinline__ int tie_fixups(const WSlice& s, uint32_t cbs, uint32_t P
 // computed before the beam is overwritten, then each output position replays
 // its segment's beam-first merge; positions are rewritten from the end and
 // every source index is <= its output.
-__device__ __noinline__ void merge_path_ties(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+__device__ __noinline__ void merge_path_ties(uint32_t* s_bidx, float* s_bdist, uint32_t* s_cidx, float* s_cdist,
+                                             uint32_t* s_pos, uint16_t* s_split, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
                                              uint32_t p0, int lane) {
+    WSlice s;
+    s.bidx = s_bidx;
+    s.bdist = s_bdist;
+    s.cidx = s_cidx;
+    s.cdist = s_cdist;
+    s.pos = s_pos;
+    s.split = s_split;
     uint32_t* bidx = s.bidx;
     float* bdist = s.bdist;
     const uint32_t first_chunk = p0 & ~31u;
@@ -547,10 +565,10 @@ __device__ __noinline__ void merge_path_ties(const WSlice& s, uint32_t cbs, uint
 
 // -------------------------------------------------------------- the search
 // Visited-set reset to the beam's nodes (src/adaptive_search.cuh:129-133).
-__device__ __noinline__ void restore_visited(const WSlice& s, uint32_t slots, int beam, int lane) {
-    w_clear(s.hash, slots, lane);
+__device__ __noinline__ void restore_visited(uint32_t* hash, const uint32_t* bidx, uint32_t slots, int beam, int lane) {
+    w_clear(hash, slots, lane);
     __syncwarp();
-    for (int i = lane; i < beam; i += 32) w_insert(s.hash, slots, s.bidx[i] & ~kMsb);
+    for (int i = lane; i < beam; i += 32) w_insert(hash, slots, bidx[i] & ~kMsb);
     __syncwarp();
 }
 
@@ -617,7 +635,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
 
     // ---------------------------------------------------------------- loop
     for (int iter = 0; iter < MAX_ITERATIONS; ++iter) {
-        if ((iter + 1) % SMALL_HASH_RESET_INTERVAL == 0) restore_visited(s, slots, beam, lane);
+        if ((iter + 1) % SMALL_HASH_RESET_INTERVAL == 0) restore_visited(s.hash, s.bidx, slots, beam, lane);
         if (iter >= pl.max_iter) break;
 
         // merge the previous iteration's candidates (:142-145)
