@@ -21,9 +21,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import threading
 import time
 
@@ -65,59 +63,71 @@ def _max_over_ranks(x: float, ws: int) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every
+    few milliseconds while the timed region runs (read-only queries), so that
+    even a short region gets samples; nvidia-smi is the fallback."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._handle = None
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = None
+    def _open(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        p = torch.cuda.get_device_properties(self.cuda_index)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        return pynvml, h
+
+    def _run(self):
+        nv, h = self._nv, self._handle
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap,
+                "hw_power_brake_slowdown": nv.nvmlClocksEventReasonHwPowerBrakeSlowdown}
+        while True:
+            try:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for n, bit in bits.items():
+                    if r & bit:
+                        self.reasons.add(n)
+            except Exception:
+                break
+            if self._stop.wait(self.period):
+                break
 
     def __enter__(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            self._nv, self._handle = self._open()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._thread = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
 
     def summary(self):
-        if not self.path or not os.path.exists(self.path):
+        if not self.samples:
             return None
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.path) as f:
-            for line in f:
-                p = [x.strip() for x in line.split(",")]
-                if len(p) < 9:
-                    continue
-                try:
-                    sm.append(float(p[1]))
-                    mx.append(float(p[2]))
-                except ValueError:
-                    continue
-                for n, v in zip(names, p[5:9]):
-                    if v.lower().startswith("active"):
-                        reasons.add(n)
-        os.unlink(self.path)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml"}
 
 
 def _peaks():
@@ -181,6 +191,9 @@ def run_flashgann(args, ws, rank, local):
     if rank != 0:
         ds = builder.materialize(args.config, device=dev)
     spec = ds.spec
+    if args.queries:
+        ds.queries = ds.queries[:args.queries]
+        ds.gt = ds.gt[:args.queries]
     K, nq = spec.K, len(ds.queries)
     qg = fg.QuantizationGraph(spec.n, spec.dim, spec.degree, ds.codebook_path, device=local)
     dq = torch.from_numpy(ds.queries).to(dev)
@@ -329,6 +342,8 @@ def main():
     ap.add_argument("--beam", type=int, default=0, help="fixed beam (default: calibrate to recall 0.95)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--queries", type=int, default=0,
+                    help="search only the first N queries of the batch (small cases for profiler captures)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     ws, rank, local = _dist()
