@@ -160,16 +160,15 @@ __device__ __forceinline__ void w_clear(uint32_t* t, uint32_t slots, int lane) {
 // Distance of one row, query dimensions lane, lane+32, ... in registers:
 // the reference's lane-strided fused accumulation and shfl_down tree
 // (include/utils.cuh:270-305).
-template <int W>
-__device__ __forceinline__ float dist_one(const float* __restrict__ r, const float (&q)[W], int dim, int use_ip,
-                                          int lane) {
+template <int W, bool IP>
+__device__ __forceinline__ float dist_one(const float* __restrict__ r, const float (&q)[W], int dim, int lane) {
     float acc = 0.0f;
 #pragma unroll
     for (int k = 0; k < W; ++k) {
         const int d = lane + 32 * k;
         if (d < dim) {
             const float x = __ldg(r + d);
-            if (use_ip) {
+            if (IP) {
                 acc = __fmaf_rn(q[k], x, acc);
             } else {
                 const float df = __fsub_rn(q[k], x);
@@ -178,7 +177,7 @@ __device__ __forceinline__ float dist_one(const float* __restrict__ r, const flo
         }
     }
     const float s = tree_sum(acc);
-    return use_ip ? -s : s;
+    return IP ? -s : s;
 }
 
 // Exact distances of G rows nd[0..G) (the last rows of a short round repeat
@@ -189,9 +188,9 @@ __device__ __forceinline__ float dist_one(const float* __restrict__ r, const flo
 // lane v+o to that of v, and while a lane still holds several rows it keeps
 // half of them and trades the other half with lane l^o.  Every sum is formed
 // from the same two operands as in the reference's tree.
-template <int W, int G>
+template <int W, int G, bool IP>
 __device__ __forceinline__ void eval_round(const float* __restrict__ rows, uint64_t rowf, int dim, const float (&q)[W],
-                                           int use_ip, const uint32_t (&nd)[G], int valid, float* out,
+                                           const uint32_t (&nd)[G], int valid, float* out,
                                            const uint32_t* slot, int e0, int lane) {
     constexpr int LG = G == 32 ? 5 : G == 16 ? 4 : G == 8 ? 3 : G == 4 ? 2 : G == 2 ? 1 : 0;
     static_assert((1 << LG) == G, "G must be a power of two <= 32");
@@ -209,7 +208,7 @@ __device__ __forceinline__ void eval_round(const float* __restrict__ rows, uint6
 #pragma unroll
         for (int k = 0; k < W; ++k) {
             const float df = __fsub_rn(q[k], x[r][k]);
-            acc[r] = use_ip ? __fmaf_rn(q[k], x[r][k], acc[r]) : __fmaf_rn(df, df, acc[r]);
+            acc[r] = IP ? __fmaf_rn(q[k], x[r][k], acc[r]) : __fmaf_rn(df, df, acc[r]);
         }
     }
 #pragma unroll
@@ -231,29 +230,37 @@ __device__ __forceinline__ void eval_round(const float* __restrict__ rows, uint6
     const int r = lane >> (5 - LG);
     if ((lane & ((1 << (5 - LG)) - 1)) == 0 && r < valid) {
         const int e = e0 + r;
-        out[slot ? slot[e] : e] = use_ip ? -acc[0] : acc[0];
+        out[slot ? slot[e] : e] = IP ? -acc[0] : acc[0];
     }
 }
 
 // Exact distances of nodes[0..n) into out[slot ? slot[e] : e]: rounds of
 // GB rows, and one round of GB/2 rows for a remainder that fits it.
-template <int W, int GB>
+template <int W, int GB, bool IP>
 __device__ __forceinline__ void eval_nodes(const float* __restrict__ rows, uint64_t rowf, int dim, const float (&q)[W],
-                                           int use_ip, const uint32_t* nodes, int n, float* out, const uint32_t* slot,
+                                           const uint32_t* nodes, int n, float* out, const uint32_t* slot,
                                            int lane) {
     int e0 = 0;
     for (; n - e0 > GB / 2; e0 += GB) {
         uint32_t nd[GB];
 #pragma unroll
         for (int r = 0; r < GB; ++r) nd[r] = nodes[e0 + r < n ? e0 + r : n - 1];
-        eval_round<W, GB>(rows, rowf, dim, q, use_ip, nd, n - e0, out, slot, e0, lane);
+        eval_round<W, GB, IP>(rows, rowf, dim, q, nd, n - e0, out, slot, e0, lane);
     }
     if (e0 < n) {
         uint32_t nd[GB / 2];
 #pragma unroll
         for (int r = 0; r < GB / 2; ++r) nd[r] = nodes[e0 + r < n ? e0 + r : n - 1];
-        eval_round<W, GB / 2>(rows, rowf, dim, q, use_ip, nd, n - e0, out, slot, e0, lane);
+        eval_round<W, GB / 2, IP>(rows, rowf, dim, q, nd, n - e0, out, slot, e0, lane);
     }
+}
+
+// min(rho keep, BUFFER_BOUND / theta budget) of keep_for, before its cutoff clamp.
+__device__ __forceinline__ int keep_cap(uint32_t active, int theta, float rho) {
+    const int ac = static_cast<int>(active);
+    const int rho_keep = static_cast<int>(keep_per_parent(active, rho));
+    const int budget = clamp_i(static_cast<int>(c_bound[theta]), 1, ac);
+    return rho_keep < budget ? rho_keep : budget;
 }
 
 // L2 prefetch of a row's raw vector (128-byte lines).
@@ -572,7 +579,7 @@ __device__ __noinline__ void restore_visited(uint32_t* hash, const uint32_t* bid
     __syncwarp();
 }
 
-template <int W, int MERGE>
+template <int W, int MERGE, bool IP>
 __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& pl, const WSlice& s,
                                              const uint16_t* bnd, uint32_t qid, bool vec, int lane) {
     constexpr bool mp = MERGE == 0;
@@ -613,7 +620,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
     s.cdist[lane] = FLT_MAX;
     __syncwarp();
     // entry point into candidate slot 0 (src/adaptive_search.cuh:110-118)
-    const float ed = dist_one<W>(rows + static_cast<uint64_t>(a.entry) * rowf, qr, dim, a.use_ip, lane);
+    const float ed = dist_one<W, IP>(rows + static_cast<uint64_t>(a.entry) * rowf, qr, dim, lane);
     if (lane == 0) {
         s.cidx[0] = a.entry;
         s.cdist[0] = ed;
@@ -773,7 +780,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
             __syncwarp();
             const int ne = __popc(ib);
             c_eval += ne;
-            eval_nodes<W, G>(rows, rowf, dim, qr, a.use_ip, s.stage, ne, s.cdist, s.eslot, lane);
+            eval_nodes<W, G, IP>(rows, rowf, dim, qr, s.stage, ne, s.cdist, s.eslot, lane);
             __syncwarp();
         } else {
             // ----------------------- speculative expanders (src/adaptive_search.cuh:344-444)
@@ -781,6 +788,8 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
             // lookup of the iteration happens before its inserts.
             const uint32_t active = static_cast<uint32_t>(deg) < 32u ? static_cast<uint32_t>(deg) : 32u;
             const int keep0 = keep_for(active, th, rho, false, 0);
+            // keep_for(active, th, rho, cut, near) = clamp(cut ? clamp(near, 1, cap) : cap, 1, active)
+            const int cap = keep_cap(active, th, rho);
             // one parent per step; the next parent's block is loaded while
             // this one is examined (the last step reloads its own block)
             ParentLane<W> cur;
@@ -809,8 +818,9 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
                         valid = isfinite(est);
                     }
                     n_est += raw_valid;
-                    const uint32_t near = __popc(__ballot_sync(kFull, valid && cut_ok && est <= cutoff));
-                    const int eff = keep_for(active, th, rho, cut_ok, near);
+                    const int near = __popc(__ballot_sync(kFull, valid && cut_ok && est <= cutoff));
+                    int eff = cut_ok ? (near < 1 ? 1 : (near > cap ? cap : near)) : cap;
+                    eff = eff < 1 ? 1 : (eff > static_cast<int>(active) ? static_cast<int>(active) : eff);
                     kl = keep_smallest(est, valid, eff, lane);
                 }
                 const uint32_t kb = __ballot_sync(kFull, kl);
@@ -836,7 +846,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
             if (ins && slot < pl.collect_cap) s.cidx[slot] = child;
             __syncwarp();
             c_eval += ne;
-            eval_nodes<W, G>(rows, rowf, dim, qr, a.use_ip, s.cidx, static_cast<int>(ne), s.cdist, nullptr, lane);
+            eval_nodes<W, G, IP>(rows, rowf, dim, qr, s.cidx, static_cast<int>(ne), s.cdist, nullptr, lane);
             __syncwarp();
         }
     }
@@ -865,7 +875,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
     __syncwarp();
 }
 
-template <int W, int MERGE>
+template <int W, int MERGE, bool IP>
 __global__ void __launch_bounds__(kWarpsPerCta * 32, kMinCtas) search_warp_kernel(const SearchArgs a, const WPlan pl,
                                                                                   int vec_codes) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -884,28 +894,32 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, kMinCtas) search_warp_kerne
         if (lane == 0) qid = atomicAdd(a.work_counter, 1u);
         qid = __shfl_sync(kFull, qid, 0);
         if (qid >= static_cast<uint32_t>(a.nq)) break;
-        search_query<W, MERGE>(a, pl, s, bnd, qid, vec_codes != 0, lane);
+        search_query<W, MERGE, IP>(a, pl, s, bnd, qid, vec_codes != 0, lane);
     }
 }
 
-template <int W>
+template <int W, bool IP>
 const void* pick_merge_w(int merge) {
     switch (merge) {
-        case 1: return reinterpret_cast<const void*>(search_warp_kernel<W, 1>);
-        case 2: return reinterpret_cast<const void*>(search_warp_kernel<W, 2>);
-        case 4: return reinterpret_cast<const void*>(search_warp_kernel<W, 4>);
-        default: return reinterpret_cast<const void*>(search_warp_kernel<W, 0>);
+        case 1: return reinterpret_cast<const void*>(search_warp_kernel<W, 1, IP>);
+        case 2: return reinterpret_cast<const void*>(search_warp_kernel<W, 2, IP>);
+        case 4: return reinterpret_cast<const void*>(search_warp_kernel<W, 4, IP>);
+        default: return reinterpret_cast<const void*>(search_warp_kernel<W, 0, IP>);
     }
 }
 
-const void* warp_kernel_for(int W, int merge) {
+template <bool IP>
+const void* pick_w(int W, int merge) {
     switch (W) {
-        case 1: return pick_merge_w<1>(merge);
-        case 2: return pick_merge_w<2>(merge);
-        case 4: return pick_merge_w<4>(merge);
-        default: return pick_merge_w<8>(merge);
+        case 1: return pick_merge_w<1, IP>(merge);
+        case 2: return pick_merge_w<2, IP>(merge);
+        case 4: return pick_merge_w<4, IP>(merge);
+        default: return pick_merge_w<8, IP>(merge);
     }
 }
+
+// kernel for W = padded dim / 32, the beam merge and the metric
+const void* warp_kernel_for(int W, int merge, bool ip) { return ip ? pick_w<true>(W, merge) : pick_w<false>(W, merge); }
 
 }  // namespace
 
@@ -935,7 +949,7 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
         snprintf(err, errlen, "shared memory %zu exceeds the device limit %d", p->smem_bytes, max_smem);
         return FG_ERR_UNSUPPORTED;
     }
-    const void* fn = warp_kernel_for(D / 32, p->merge_n2);
+    const void* fn = warp_kernel_for(D / 32, p->merge_n2, a.use_ip != 0);
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p->smem_bytes));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
@@ -969,7 +983,7 @@ cudaError_t launch_search_warp(const SearchArgs& a, const SearchPlan& p, cudaStr
     pl.slice = static_cast<uint32_t>(p.slice_bytes);
     cudaError_t e = cudaMemsetAsync(a.work_counter, 0, sizeof(uint32_t), stream);
     if (e != cudaSuccess) return e;
-    const void* fn = warp_kernel_for(a.padded_dim / 32, p.merge_n2);
+    const void* fn = warp_kernel_for(a.padded_dim / 32, p.merge_n2, a.use_ip != 0);
     SearchArgs args = a;
     int vec = p.vec_codes;
     void* params[] = {&args, &pl, &vec};

@@ -77,6 +77,33 @@ def test_search_matches_oracle(name, beams):
     qg.close()
 
 
+@pytest.mark.parametrize("name,beams", [("t_4k96f", (64, 100, 256)), ("t_2k", (128, 200))])
+def test_inner_product_search_matches_oracle(name, beams):
+    """METRIC_IP (the reference's Text2Image path, negated dot products) on a
+    normalised 96-d set (padded to D = 128) and an integer 128-d set."""
+    import oracle
+    import flashgann_b200 as fg
+    ds = dataset(name)
+    qg = fg.QuantizationGraph.from_arrays(ds.rows, ds.signs, ds.entry, ds.spec.dim, ds.spec.degree,
+                                          metric=fg.METRIC_IP)
+    oi = oracle.OracleIndex(ds.rows, ds.signs, ds.entry, ds.spec.dim, ds.spec.degree, use_ip=True)
+    K = ds.spec.K
+    nq = min(len(ds.queries), 100)
+    for beam in beams:
+        g = _run_gpu(qg, ds.queries[:nq], K, beam, trace_cap=160)
+        bad = []
+        for i in range(nq):
+            o = oi.search_one(ds.queries[i], K, beam, trace_cap=160)
+            same = (np.array_equal(o["ids"], g["ids"][i]) and
+                    np.array_equal(o["dists"].view(np.uint32), g["dists"][i].view(np.uint32)))
+            n = len(o["trace_count"])
+            same = same and np.array_equal(o["trace"], g["trace"][i, :n])
+            if not same:
+                bad.append(i)
+        assert not bad, f"{name} IP beam {beam}: {len(bad)} queries differ, first {bad[:5]}"
+    qg.close()
+
+
 def test_host_buffer_api_matches_device_api():
     import flashgann_b200 as fg
     ds, qg = _gpu_index("t_2k")
