@@ -122,6 +122,11 @@ SPECS = {
                            (100, 256), seed=13, kind="norm_aniso"),
     "t_2k": DatasetSpec("t_2k", 2_000, 64, 128, 4, 25.0, 0.0, 255.0, 32, 100,
                         (32, 100, 128, 200, 256), seed=14),
+    # padded dimensions above 256 (the one-CTA-per-query kernel): 300 -> 512, 1536 -> 2048
+    "t_2k300": DatasetSpec("t_2k300", 2_000, 48, 300, 4, 25.0, 0.0, 255.0, 32, 100,
+                           (100, 256), seed=15),
+    "t_1k1536": DatasetSpec("t_1k1536", 1_000, 24, 1536, 1, 0.0, 0.0, 0.0, 32, 10,
+                            (32, 128), seed=16, kind="lowrank"),
 }
 
 
@@ -161,6 +166,25 @@ def generate_vectors(spec: DatasetSpec) -> Tuple[np.ndarray, np.ndarray]:
             v = centres[lab] + r.standard_normal((m, spec.dim)) * scales[lab]
             v /= np.linalg.norm(v, axis=1, keepdims=True)
             return v.astype(np.float32)
+
+        return draw(1, spec.n), draw(2, spec.nq)
+    if spec.kind == "lowrank":
+        # rank-64 latent x a fixed 64 x dim map + N(0, 0.02^2), L2-normalised
+        cr = _rng(spec.seed, 0)
+        rank = 64
+        basis = cr.standard_normal((rank, spec.dim)).astype(np.float32) / np.float32(np.sqrt(rank))
+
+        def draw(stream: int, m: int) -> np.ndarray:
+            r = _rng(spec.seed, stream)
+            out = np.empty((m, spec.dim), dtype=np.float32)
+            step = 1 << 16
+            for s0 in range(0, m, step):
+                e = min(m, s0 + step)
+                z = r.standard_normal((e - s0, rank), dtype=np.float32)
+                v = z @ basis + r.standard_normal((e - s0, spec.dim), dtype=np.float32) * np.float32(0.02)
+                v /= np.linalg.norm(v, axis=1, keepdims=True)
+                out[s0:e] = v
+            return out
 
         return draw(1, spec.n), draw(2, spec.nq)
     raise ValueError(f"unknown dataset kind {spec.kind}")

@@ -234,24 +234,18 @@ __device__ __forceinline__ void eval_round(const float* __restrict__ rows, uint6
     }
 }
 
-// Exact distances of nodes[0..n) into out[slot ? slot[e] : e]: rounds of
-// GB rows, and one round of GB/2 rows for a remainder that fits it.
+// Exact distances of nodes[0..n) into out[slot ? slot[e] : e], GB rows per round
+// (one round shape keeps the loop small for the instruction cache).
 template <int W, int GB, bool IP>
 __device__ __forceinline__ void eval_nodes(const float* __restrict__ rows, uint64_t rowf, int dim, const float (&q)[W],
                                            const uint32_t* nodes, int n, float* out, const uint32_t* slot,
                                            int lane) {
     int e0 = 0;
-    for (; n - e0 > GB / 2; e0 += GB) {
+    for (; e0 < n; e0 += GB) {
         uint32_t nd[GB];
 #pragma unroll
         for (int r = 0; r < GB; ++r) nd[r] = nodes[e0 + r < n ? e0 + r : n - 1];
         eval_round<W, GB, IP>(rows, rowf, dim, q, nd, n - e0, out, slot, e0, lane);
-    }
-    if (e0 < n) {
-        uint32_t nd[GB / 2];
-#pragma unroll
-        for (int r = 0; r < GB / 2; ++r) nd[r] = nodes[e0 + r < n ? e0 + r : n - 1];
-        eval_round<W, GB / 2, IP>(rows, rowf, dim, q, nd, n - e0, out, slot, e0, lane);
     }
 }
 
@@ -275,17 +269,17 @@ __device__ __forceinline__ void prefetch_row(const float* r, int dim) {
 // and returns p0 = #{beam < cand[0]}, the first position that can change.
 // Stable (beam-first) merge in place: output o >= p0 is candidate m if
 // pos[m] == o, else beam[o - #{pos < o}].  Chunks of 32 positions are
-// rewritten from the end, four per step (all reads of a step before its
+// rewritten from the end, two per step (all reads of a step before its
 // writes; every source index is <= its output, so lower chunks are intact).
 __device__ __forceinline__ void stable_shift(uint32_t* bidx, float* bdist, float k, uint32_t v, uint32_t pos, uint32_t P,
                                              uint32_t p0, int lane) {
     const int first = static_cast<int>(p0 & ~31u);
-    for (int g = static_cast<int>((P - 1) & ~31u); g >= first; g -= 128) {
-        float od[4];
-        uint32_t ov[4];
-        bool act[4];
+    for (int g = static_cast<int>((P - 1) & ~31u); g >= first; g -= 64) {
+        float od[2];
+        uint32_t ov[2];
+        bool act[2];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 2; ++u) {
             const int c0 = g - 32 * u;
             act[u] = false;
             od[u] = 0.0f;
@@ -313,7 +307,7 @@ __device__ __forceinline__ void stable_shift(uint32_t* bidx, float* bdist, float
         }
         __syncwarp();
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 2; ++u) {
             if (act[u]) {
                 const uint32_t o = static_cast<uint32_t>(g - 32 * u) + lane;
                 bdist[o] = od[u];
