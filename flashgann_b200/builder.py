@@ -566,3 +566,56 @@ def materialize(name_or_spec, cache_dir: Optional[str] = None, device=None,
     if verbose:
         print(f"[builder] {spec.name}: done {time.time() - t0:.1f}s", flush=True)
     return Dataset(spec, base, queries, gt, rows, signs, entry, L, paths["cb"], d)
+
+
+# --------------------------------------------------------------------------
+# index shards (every GPU holds one shard with its
+# own graph and entry point; global id = shard offset + local id)
+# --------------------------------------------------------------------------
+@dataclasses.dataclass
+class Shard:
+    spec: DatasetSpec
+    index: int
+    count: int
+    offset: int           # global id of local node 0
+    n: int
+    queries: np.ndarray   # the full query batch
+    gt: np.ndarray        # global exact neighbours of the full base
+    rows: np.ndarray
+    signs: np.ndarray
+    entry: int
+    layout: Layout
+    codebook_path: str
+
+
+def shard_range(n: int, count: int, index: int) -> Tuple[int, int]:
+    base, extra = divmod(n, count)
+    start = index * base + min(index, extra)
+    return start, start + base + (1 if index < extra else 0)
+
+
+def materialize_shard(name_or_spec, index: int, count: int, cache_dir: Optional[str] = None, device=None,
+                      verbose: bool = False) -> Shard:
+    """Shard `index` of `count` contiguous slices of a dataset's base vectors,
+    with its own graph (built on the slice only), entry point and codebook;
+    the signs are the dataset's.  The full dataset is materialised first (it
+    provides the vectors and the global ground truth)."""
+    spec = SPECS[name_or_spec] if isinstance(name_or_spec, str) else name_or_spec
+    full = materialize(spec, cache_dir=cache_dir, device=device, verbose=verbose)
+    s, e = shard_range(spec.n, count, index)
+    L = full.layout
+    d = os.path.join(cache_dir or default_cache_dir(), f"{spec.name}_shard{index}of{count}")
+    os.makedirs(d, exist_ok=True)
+    cb = os.path.join(d, "qg_codebook.index")
+    if os.path.exists(cb):
+        entry, rows, signs = read_codebook(cb, e - s, spec.dim, spec.degree)
+    else:
+        part = full.base[s:e]
+        nbrs, entry = build_graph(part, spec.degree, spec.seed * 1000 + index, knn_k=spec.knn_k, device=device)
+        signs = full.signs
+        rows = encode_rows(part, nbrs, signs, device=device)
+        write_codebook(cb + ".tmp", entry, rows, signs)
+        os.replace(cb + ".tmp", cb)
+        if verbose:
+            print(f"[builder] {spec.name} shard {index}/{count}: {e - s} nodes", flush=True)
+    return Shard(spec, index, count, s, e - s, full.queries, full.gt, rows, signs, entry, L, cb)

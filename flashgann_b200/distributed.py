@@ -98,6 +98,24 @@ def search_sharded(search: Callable[[np.ndarray], Tuple[np.ndarray, np.ndarray]]
     return mi.cpu().numpy().astype(np.uint32), md.cpu().numpy()
 
 
+def gather_shard_topk(ids: torch.Tensor, dists: torch.Tensor, K: int, shard_offset: int,
+                      group=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Device-side merge for a sharded index: this rank's per-query top-K
+    (local ids [nq, K] int32 / uint32 bits, dists [nq, K] f32, on this rank's
+    device) are offset to global ids, all-gathered (NCCL over NVLink on GPUs)
+    and merged into the global top-K on every rank.  Returns (ids int64,
+    dists f32), both [nq, K] on the input device."""
+    world = dist.get_world_size(group)
+    gi = (ids.to(torch.int64) & 0xFFFFFFFF) + int(shard_offset)
+    gd = dists.contiguous()
+    nq, k = gi.shape
+    all_i = torch.empty((world * nq, k), dtype=gi.dtype, device=gi.device)
+    all_d = torch.empty((world * nq, k), dtype=gd.dtype, device=gd.device)
+    dist.all_gather_into_tensor(all_i, gi, group=group)
+    dist.all_gather_into_tensor(all_d, gd, group=group)
+    return merge_shard_topk(all_d.view(world, nq, k), all_i.view(world, nq, k), K)
+
+
 def max_over_ranks(x: float, group=None) -> float:
     """Device-timed step time: the slowest rank's."""
     if not dist.is_initialized() or dist.get_world_size(group) == 1:

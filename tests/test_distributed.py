@@ -65,6 +65,38 @@ def test_two_rank_search_equals_single_process(mode, tmp_path):
     assert float(r["t"]) == 2.0
 
 
+def _gather_worker(rank, world, port, out_path):
+    import torch
+    import torch.distributed as dist
+    from flashgann_b200 import distributed as fgd
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    rng = np.random.default_rng(1)
+    base = np.rint(rng.uniform(0, 255, size=(500, 8))).astype(np.float32)
+    queries = np.rint(rng.uniform(0, 255, size=(21, 8))).astype(np.float32)
+    s, e = fgd.partition(base.shape[0], world, rank)
+    ids, d = _brute(base[s:e], 7)(queries)
+    gi, gd = fgd.gather_shard_topk(torch.from_numpy(ids.view(np.int32)), torch.from_numpy(d), 7, s)
+    if rank == 0:
+        np.savez(out_path, ids=gi.numpy(), d=gd.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_device_shard_merge_equals_single_index(tmp_path):
+    out = str(tmp_path / "g.npz")
+    mp.spawn(_gather_worker, args=(3, _free_port(), out), nprocs=3, join=True)
+    r = np.load(out)
+    rng = np.random.default_rng(1)
+    base = np.rint(rng.uniform(0, 255, size=(500, 8))).astype(np.float32)
+    queries = np.rint(rng.uniform(0, 255, size=(21, 8))).astype(np.float32)
+    ids, d = _brute(base, 7)(queries)
+    assert np.array_equal(r["d"], d)
+    for i in range(len(ids)):
+        assert sorted(zip(r["d"][i].tolist(), r["ids"][i].tolist())) == sorted(zip(d[i].tolist(), ids[i].tolist()))
+
+
 def test_partition_covers_everything():
     for n in (0, 1, 7, 10000):
         for w in (1, 2, 3, 8):
