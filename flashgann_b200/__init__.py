@@ -32,6 +32,7 @@ __all__ = [
     "QuantizationGraph", "FlashGANNError", "QueryStats", "lib", "load_fvecs", "load_ivecs", "compute_recall",
     "append_run_stats_to_csv", "infer_metric_from_dataset_path", "effective_sort_beam_size", "METRIC_L2",
     "METRIC_IP",
+    "search_multi",
 ]
 
 
@@ -150,6 +151,25 @@ class QuantizationGraph:
 
     def __exit__(self, *exc):
         self.close()
+
+
+
+def search_multi(graphs, queries: np.ndarray, K: int, beam: int, with_dists: bool = False):
+    """One batch over several QuantizationGraph handles of the same codebook,
+    each on its own device (fg_search_multi): the batch is split into balanced
+    contiguous slices searched concurrently.  Returns (ids uint32 [nq, K],
+    dists float32 [nq, K] or None, elapsed seconds)."""
+    q = np.ascontiguousarray(queries, dtype=np.float32)
+    nq = q.shape[0]
+    hs = (ctypes.c_void_p * len(graphs))(*[g._h.value for g in graphs])
+    ids = np.empty((nq, K), dtype=np.uint32)
+    dists = np.empty((nq, K), dtype=np.float32) if with_dists else None
+    el = ctypes.c_double()
+    _check(lib().fg_search_multi(hs, len(graphs), nq, q.ctypes.data_as(ctypes.c_void_p), K,
+                                 ids.ctypes.data_as(ctypes.c_void_p),
+                                 dists.ctypes.data_as(ctypes.c_void_p) if with_dists else None, beam,
+                                 ctypes.byref(el)), "fg_search_multi")
+    return ids, dists, el.value
 
 
 def effective_sort_beam_size(beam: int) -> int:

@@ -59,6 +59,7 @@ SIGNATURES = [
     ("fg_index_set_metric", ctypes.c_int, [_vp, _i32]),
     ("fg_search", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _i32, ctypes.POINTER(_f64)]),
     ("fg_search_noalloc", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _i32, ctypes.POINTER(_f64)]),
+    ("fg_search_multi", ctypes.c_int, [ctypes.POINTER(_vp), _i32, _i32, _vp, _i32, _vp, _vp, _i32, ctypes.POINTER(_f64)]),
     ("fg_search_device", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp]),
     ("fg_search_device_ex", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _i32]),
     ("fg_query_prepare_device", ctypes.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),

@@ -31,6 +31,8 @@ struct fg_index {
     size_t cap_queries = 0;
     uint32_t* d_results = nullptr;
     size_t cap_results = 0;
+    float* d_dists = nullptr;  // fg_search_multi with distances
+    size_t cap_dists = 0;
     uint32_t* d_counter = nullptr;  // persistent-CTA work counter
     cudaStream_t stream = nullptr;
 };
@@ -154,6 +156,7 @@ void destroy(fg_index* x) {
     if (x->d_signs) cudaFree(x->d_signs);
     if (x->d_queries) cudaFree(x->d_queries);
     if (x->d_results) cudaFree(x->d_results);
+    if (x->d_dists) cudaFree(x->d_dists);
     if (x->d_counter) cudaFree(x->d_counter);
     if (x->stream) cudaStreamDestroy(x->stream);
     delete x;
@@ -164,6 +167,19 @@ int check_device(int device) {
     cudaError_t e = cudaGetDeviceCount(&count);
     if (e != cudaSuccess || count < 1) return fail(FG_ERR_NO_DEVICE, "no CUDA device available (%s)", cudaGetErrorString(e));
     if (device < 0 || device >= count) return fail(FG_ERR_ARG, "device %d outside [0, %d)", device, count);
+    return FG_OK;
+}
+
+// Grows a device buffer of the host-buffer search paths to hold n elements.
+template <typename T>
+int grow(T** buf, size_t* cap, size_t n, const char* what) {
+    if (n <= *cap) return FG_OK;
+    if (*buf) cudaFree(*buf);
+    *buf = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMalloc(buf, n * sizeof(T));
+    if (e != cudaSuccess) return fail(FG_ERR_OOM, "cudaMalloc(%s): %s", what, cudaGetErrorString(e));
+    *cap = n;
     return FG_OK;
 }
 
@@ -440,6 +456,85 @@ int fg_search(fg_index* x, int32_t nq, const float* queries, int32_t K, uint32_t
     if ((e = cudaMemcpyAsync(result_idx, x->d_results, rn * sizeof(uint32_t), cudaMemcpyDeviceToHost, x->stream)) != cudaSuccess)
         return cuda_fail(e, "cudaMemcpyAsync(results)");
     if ((e = cudaStreamSynchronize(x->stream)) != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    return FG_OK;
+}
+
+int fg_search_multi(fg_index* const* indexes, int32_t count, int32_t nq, const float* queries, int32_t K,
+                    uint32_t* result_idx, float* result_dist, int32_t beam, double* elapsed_s) {
+    g_err.clear();
+    if (!indexes || count < 1) return fail(FG_ERR_ARG, "need at least one index");
+    if (nq < 0) return fail(FG_ERR_ARG, "nq must be >= 0 (got %d)", nq);
+    if (nq > 0 && (!queries || !result_idx)) return fail(FG_ERR_ARG, "null query or result buffer");
+    if (elapsed_s) *elapsed_s = 0.0;
+    const fg_index* x0 = indexes[0];
+    for (int i = 0; i < count; ++i) {
+        const fg_index* x = indexes[i];
+        if (!x) return fail(FG_ERR_ARG, "null index %d", i);
+        if (x->n != x0->n || x->dim != x0->dim || x->degree != x0->degree || x->metric != x0->metric ||
+            x->entry != x0->entry)
+            return fail(FG_ERR_ARG, "index %d does not hold the same graph as index 0", i);
+    }
+    std::vector<fg::SearchArgs> args(count);
+    std::vector<fg::SearchPlan> plans(count);
+    std::vector<int> lo(count), hi(count);
+    const int per = nq / count, extra = nq % count;
+    for (int i = 0; i < count; ++i) {
+        lo[i] = i * per + (i < extra ? i : extra);
+        hi[i] = lo[i] + per + (i < extra ? 1 : 0);
+    }
+    cudaError_t e;
+    int rc;
+    // copies and launches of every device first, so that the devices run concurrently
+    for (int i = 0; i < count; ++i) {
+        fg_index* x = indexes[i];
+        const int m = hi[i] - lo[i];
+        DeviceGuard g(x->device);
+        if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
+        fg::SearchArgs& a = args[i];
+        a = base_args(x);
+        a.nq = m;
+        a.K = K;
+        a.beam = beam;
+        char err[256];
+        if ((rc = fg::plan_search(a, &plans[i], x->device, err, sizeof(err))) != FG_OK) return fail(rc, "%s", err);
+        if (m == 0) continue;
+        const size_t qn = static_cast<size_t>(m) * x->dim, rn = static_cast<size_t>(m) * K;
+        if ((rc = grow(&x->d_queries, &x->cap_queries, qn, "queries")) != FG_OK) return rc;
+        if ((rc = grow(&x->d_results, &x->cap_results, rn, "results")) != FG_OK) return rc;
+        if (result_dist && (rc = grow(&x->d_dists, &x->cap_dists, rn, "distances")) != FG_OK) return rc;
+        a.queries = x->d_queries;
+        a.out_ids = x->d_results;
+        a.out_dists = result_dist ? x->d_dists : nullptr;
+        if ((e = cudaMemcpyAsync(x->d_queries, queries + static_cast<size_t>(lo[i]) * x->dim, qn * sizeof(float),
+                                 cudaMemcpyHostToDevice, x->stream)) != cudaSuccess)
+            return cuda_fail(e, "cudaMemcpyAsync(queries)");
+    }
+    const auto t0 = std::chrono::high_resolution_clock::now();
+    for (int i = 0; i < count; ++i) {
+        if (hi[i] == lo[i]) continue;
+        DeviceGuard g(indexes[i]->device);
+        if ((e = fg::launch_search(args[i], plans[i], indexes[i]->stream)) != cudaSuccess)
+            return cuda_fail(e, "search launch");
+    }
+    for (int i = 0; i < count; ++i) {
+        if (hi[i] == lo[i]) continue;
+        DeviceGuard g(indexes[i]->device);
+        if ((e = cudaStreamSynchronize(indexes[i]->stream)) != cudaSuccess) return cuda_fail(e, "search");
+    }
+    const auto t1 = std::chrono::high_resolution_clock::now();
+    if (elapsed_s) *elapsed_s = std::chrono::duration<double>(t1 - t0).count();
+    for (int i = 0; i < count; ++i) {
+        fg_index* x = indexes[i];
+        const size_t rn = static_cast<size_t>(hi[i] - lo[i]) * K;
+        if (rn == 0) continue;
+        DeviceGuard g(x->device);
+        if ((e = cudaMemcpy(result_idx + static_cast<size_t>(lo[i]) * K, x->d_results, rn * sizeof(uint32_t),
+                            cudaMemcpyDeviceToHost)) != cudaSuccess)
+            return cuda_fail(e, "cudaMemcpy(results)");
+        if (result_dist && (e = cudaMemcpy(result_dist + static_cast<size_t>(lo[i]) * K, x->d_dists,
+                                           rn * sizeof(float), cudaMemcpyDeviceToHost)) != cudaSuccess)
+            return cuda_fail(e, "cudaMemcpy(distances)");
+    }
     return FG_OK;
 }
 

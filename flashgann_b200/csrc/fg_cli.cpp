@@ -22,7 +22,7 @@ int main(int argc, char** argv) {
     if (argc < 5) {
         fprintf(stderr,
                 "Usage: %s <data.fvecs> <query.fvecs> <gt.ivecs> <qg_codebook> [K=100] [beam_size=128] [degree=32] "
-                "[-csv output.csv] [-device N]\n",
+                "[-csv output.csv] [-device N] [-gpus G]\n",
                 argv[0]);
         return 1;
     }
@@ -30,7 +30,7 @@ int main(int argc, char** argv) {
     const char* query_file = argv[2];
     const char* gt_file = argv[3];
     const char* codebook = argv[4];
-    int K = 100, beam = 128, degree = 32, device = 0;
+    int K = 100, beam = 128, degree = 32, device = 0, gpus = 1;
     std::string csv;
     int ai = 5;
     if (ai < argc && argv[ai][0] != '-') K = atoi(argv[ai++]);
@@ -42,6 +42,12 @@ int main(int argc, char** argv) {
             csv = argv[++ai];
         } else if (a == "-device" && ai + 1 < argc) {
             device = atoi(argv[++ai]);
+        } else if (a == "-gpus" && ai + 1 < argc) {
+            gpus = atoi(argv[++ai]);
+            if (gpus < 1) {
+                fprintf(stderr, "-gpus needs a count >= 1\n");
+                return 1;
+            }
         } else {
             fprintf(stderr, "Unknown argument: %s\n", a.c_str());
             return 1;
@@ -87,9 +93,18 @@ int main(int argc, char** argv) {
     if ((rc = fg_vecs_read(query_file, queries.data(), nq, qdim))) return die(rc, "queries");
     if ((rc = fg_vecs_read(gt_file, gt.data(), gt_nq, gt_k))) return die(rc, "ground truth");
 
-    fg_index* index = nullptr;
-    if ((rc = fg_index_load(codebook, n, static_cast<uint64_t>(dim), degree, metric, device, &index)))
-        return die(rc, "codebook");
+    // -gpus G: the codebook on devices device .. device+G-1, the batch split across them
+    std::vector<fg_index*> indexes(gpus, nullptr);
+    auto free_all = [&]() {
+        for (fg_index* x : indexes) fg_index_free(x);
+    };
+    for (int g = 0; g < gpus; ++g) {
+        if ((rc = fg_index_load(codebook, n, static_cast<uint64_t>(dim), degree, metric, device + g, &indexes[g]))) {
+            free_all();
+            return die(rc, "codebook");
+        }
+    }
+    fg_index* index = indexes[0];
     fg_layout L;
     fg_index_layout(index, &L);
     printf("Loaded codebook: %llu nodes, dim=%llu, degree=%d, padded_dim=%llu, row_offset=%llu floats (entry_point=%u)\n",
@@ -98,11 +113,11 @@ int main(int argc, char** argv) {
 
     std::vector<uint32_t> results(nq * static_cast<uint64_t>(K));
     double elapsed = 0.0;
-    if ((rc = fg_search(index, static_cast<int32_t>(nq), queries.data(), K, results.data(), beam, &elapsed))) {
-        fg_index_free(index);
-        return die(rc, "search");
-    }
-    fg_index_free(index);
+    rc = gpus == 1 ? fg_search(index, static_cast<int32_t>(nq), queries.data(), K, results.data(), beam, &elapsed)
+                   : fg_search_multi(indexes.data(), gpus, static_cast<int32_t>(nq), queries.data(), K, results.data(),
+                                     nullptr, beam, &elapsed);
+    free_all();
+    if (rc) return die(rc, "search");
 
     const float recall = fg_compute_recall(results.data(), gt.data(), nq, K, gt_k) * 100.0f;
     const double latency_ms = nq > 0 ? elapsed * 1000.0 / static_cast<double>(nq) : 0.0;

@@ -97,6 +97,19 @@ int fg_index_set_metric(fg_index* index, int32_t metric);
 int fg_search(fg_index* index, int32_t nq, const float* queries, int32_t K, uint32_t* result_idx, int32_t beam,
               double* elapsed_s);
 
+/* Replicated index on several devices from one host thread: `indexes` holds
+ * `count` handles of the same codebook, each loaded on its own device
+ * (fg_index_load with device = 0, 1, ...).  The batch is split into
+ * contiguous, balanced slices in handle order; every device's copies and
+ * launch are issued before any is awaited, so the devices search concurrently;
+ * result_idx[nq*K] (and result_dist[nq*K], optional) are gathered in query
+ * order.  elapsed_s (optional) = wall time from the first launch to the last
+ * device's completion, excluding the copies.  Same arguments and errors as
+ * fg_search otherwise; no counterpart in the reference (its search uses the
+ * current device only, gpu_search_adaptive.cu:30-34). */
+int fg_search_multi(fg_index* const* indexes, int32_t count, int32_t nq, const float* queries, int32_t K,
+                    uint32_t* result_idx, float* result_dist, int32_t beam, double* elapsed_s);
+
 /* Size of the fixed device scratch used by fg_search_noalloc (8 MiB). */
 #define FG_NOALLOC_SCRATCH_BYTES 8388608
 
