@@ -46,6 +46,7 @@ struct SearchPlan {
     int kernel = 0;            // 0: one CTA per query (fg_search.cu), 1: one warp per query (fg_search_warp.cu)
     uint32_t slots = 0;        // warp kernel: visited-set slots
     size_t slice_bytes = 0;    // warp kernel: shared memory per query
+    int min_ctas = 0;          // warp kernel: CTAs per SM its register budget is compiled for
     size_t smem_bytes = 0;
     int grid = 0;
     int threads = 0;

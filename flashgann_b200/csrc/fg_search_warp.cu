@@ -45,7 +45,10 @@ namespace fg {
 namespace {
 
 constexpr int kWarpsPerCta = 4;
-constexpr int kMinCtas = 4;  // 16 warps per SM: 128 registers per thread
+// Register budgets: 4 CTAs per SM (128 registers per thread) or, when the
+// query slices of 5 CTAs fit the SM's shared memory, 5 (96 registers).
+constexpr int kCtasLarge = 4;
+constexpr int kCtasSmall = 5;
 
 struct WPlan {
     uint32_t padded, cbs, collect_cap;
@@ -65,12 +68,13 @@ struct WSlice {
     uint32_t* wrap;
     uint32_t* cidx;   // candidate buffer (32 entries)
     float* cdist;
+    uint32_t* pos;    // merge path with ties: stable positions of the candidates
     uint32_t* stage;  // kept children in (parent, rank) order, or the evaluation list
     uint32_t* eslot;  // single-expander path: candidate slot of each evaluation
-    uint32_t* pos;    // merge path with ties: stable positions of the candidates
     uint32_t* pnode;  // expanders of the iteration
     float* pdist;
-    uint16_t* split;  // merge path with ties: the reference's split at each segment boundary
+    // stage and eslot (256 contiguous bytes) double as the merge's tie fix-up
+    // list, and stage as the query factors during set-up
     QueryState* qs;
 };
 
@@ -93,62 +97,96 @@ __host__ __device__ inline size_t slice_layout(uint32_t padded, uint32_t slots, 
     p = take(static_cast<size_t>(W) * 4); if (s) s->wrap = reinterpret_cast<uint32_t*>(p);
     p = take(32 * 4); if (s) s->cidx = reinterpret_cast<uint32_t*>(p);
     p = take(32 * 4); if (s) s->cdist = reinterpret_cast<float*>(p);
+    p = take(32 * 4); if (s) s->pos = reinterpret_cast<uint32_t*>(p);
     p = take(32 * 4); if (s) s->stage = reinterpret_cast<uint32_t*>(p);
     p = take(32 * 4); if (s) s->eslot = reinterpret_cast<uint32_t*>(p);
-    p = take(32 * 4); if (s) s->pos = reinterpret_cast<uint32_t*>(p);
     p = take(SEARCH_WIDTH * 4); if (s) s->pnode = reinterpret_cast<uint32_t*>(p);
     p = take(SEARCH_WIDTH * 4); if (s) s->pdist = reinterpret_cast<float*>(p);
-    p = take(mp ? (BLOCK_SIZE + 1) * 2 : 0); if (s) s->split = reinterpret_cast<uint16_t*>(p);
-    p = take(sizeof(QueryState)); if (s) s->qs = reinterpret_cast<QueryState*>(p);
+    if (s) s->qs = reinterpret_cast<QueryState*>(s->stage);
+    (void)mp;
     return off;
 }
 
 // ---------------------------------------------------------------- visited set
-// Exact set as in fg_device.cuh (buckets of 4 slots, linear probing, one
-// 128-bit load per bucket), over any multiple of 4 slots: the bucket is the
-// high word of (Fibonacci hash x bucket count).
-__device__ __forceinline__ uint32_t w_bucket(uint32_t key, uint32_t slots) {
-    return __umulhi(key * 0x9E3779B1u, slots >> 2) << 2;
+// Exact set of node ids in buckets of 4 slots (one 128-bit shared load per
+// bucket), two-choice: a key lives in the emptier of its two buckets, so a
+// lookup reads both (independent loads) and a missing key is settled as soon
+// as either has an empty slot.  Only when both are full does an insert walk on
+// linearly from the second bucket, and a lookup with both full walks the same
+// way (nothing is ever removed between resets, so the walk meets the key
+// before any empty slot).  Two choices keep the walks rare at loads up to ~93 %.
+__device__ __forceinline__ void w_buckets(uint32_t key, uint32_t nb, uint32_t& b1, uint32_t& b2) {
+    b1 = __umulhi(key * 0x9E3779B1u, nb);
+    b2 = __umulhi((key ^ 0x5bd1e995u) * 0x85EBCA77u, nb);
+    if (b2 == b1) b2 = b1 + 1 == nb ? 0 : b1 + 1;
 }
 
-__device__ __forceinline__ bool w_insert(uint32_t* t, uint32_t slots, uint32_t key) {
-    uint32_t b = w_bucket(key, slots);
-    for (uint32_t n = 0; n < slots; n += 4) {
-        const uint4 v = *reinterpret_cast<const uint4*>(t + b);
-        const uint32_t sl[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
+__device__ __forceinline__ bool has_key(const uint4& v, uint32_t key) {
+    return v.x == key || v.y == key || v.z == key || v.w == key;
+}
+
+__device__ __forceinline__ int empties(const uint4& v) {
+    return (v.x == kMax) + (v.y == kMax) + (v.z == kMax) + (v.w == kMax);
+}
+
+// the linear walk from bucket b + 1 (both of the key's buckets full)
+__device__ __noinline__ bool w_walk_contains(const uint32_t* t, uint32_t nb, uint32_t key, uint32_t b) {
+    for (uint32_t n = 1; n < nb; ++n) {
+        b = b + 1 == nb ? 0 : b + 1;
+        const uint4 v = *reinterpret_cast<const uint4*>(t + 4 * b);
+        if (has_key(v, key)) return true;
+        if (empties(v)) return false;
+    }
+    return false;
+}
+
+__device__ __noinline__ bool w_walk_insert(uint32_t* t, uint32_t nb, uint32_t key, uint32_t b) {
+    for (uint32_t n = 1; n < nb; ++n) {
+        b = b + 1 == nb ? 0 : b + 1;
         for (int j = 0; j < 4; ++j) {
-            if (sl[j] == key) return false;
-            if (sl[j] == kMax) {
-                const uint32_t old = atomicCAS(&t[b + j], kMax, key);
+            const uint32_t cur = t[4 * b + j];
+            if (cur == key) return false;
+            if (cur == kMax) {
+                const uint32_t old = atomicCAS(&t[4 * b + j], kMax, key);
                 if (old == kMax) return true;
                 if (old == key) return false;
             }
         }
-        b += 4;
-        if (b >= slots) b = 0;
     }
     return false;
 }
 
-__device__ __noinline__ bool w_contains_probe(const uint32_t* t, uint32_t slots, uint32_t key, uint32_t b) {
-    for (uint32_t n = 4; n < slots; n += 4) {
-        b += 4;
-        if (b >= slots) b = 0;
-        const uint4 v = *reinterpret_cast<const uint4*>(t + b);
-        if (v.x == key || v.y == key || v.z == key || v.w == key) return true;
-        if (v.x == kMax || v.y == kMax || v.z == kMax || v.w == kMax) return false;
+// true if the key was not in the set (other lanes may insert concurrently)
+__device__ __forceinline__ bool w_insert(uint32_t* t, uint32_t slots, uint32_t key) {
+    const uint32_t nb = slots >> 2;
+    uint32_t b1, b2;
+    w_buckets(key, nb, b1, b2);
+    for (uint32_t tries = 0; tries < slots; ++tries) {
+        const uint4 v1 = *reinterpret_cast<const uint4*>(t + 4 * b1);
+        const uint4 v2 = *reinterpret_cast<const uint4*>(t + 4 * b2);
+        if (has_key(v1, key) || has_key(v2, key)) return false;
+        const int e1 = empties(v1), e2 = empties(v2);
+        if (e1 == 0 && e2 == 0) return w_walk_insert(t, nb, key, b2);
+        const uint32_t b = e1 >= e2 ? b1 : b2;
+        const uint4 v = e1 >= e2 ? v1 : v2;
+        const int j = v.x == kMax ? 0 : v.y == kMax ? 1 : v.z == kMax ? 2 : 3;
+        const uint32_t old = atomicCAS(&t[4 * b + j], kMax, key);
+        if (old == kMax) return true;
+        if (old == key) return false;
+        // another lane took the slot: look again
     }
     return false;
 }
 
-// first bucket inline; a full bucket without the key continues out of line
 __device__ __forceinline__ bool w_contains(const uint32_t* t, uint32_t slots, uint32_t key) {
-    const uint32_t b = w_bucket(key, slots);
-    const uint4 v = *reinterpret_cast<const uint4*>(t + b);
-    if (v.x == key || v.y == key || v.z == key || v.w == key) return true;
-    if (v.x == kMax || v.y == kMax || v.z == kMax || v.w == kMax) return false;
-    return w_contains_probe(t, slots, key, b);
+    const uint32_t nb = slots >> 2;
+    uint32_t b1, b2;
+    w_buckets(key, nb, b1, b2);
+    const uint4 v1 = *reinterpret_cast<const uint4*>(t + 4 * b1);
+    const uint4 v2 = *reinterpret_cast<const uint4*>(t + 4 * b2);
+    if (has_key(v1, key) || has_key(v2, key)) return true;
+    if (empties(v1) || empties(v2)) return false;
+    return w_walk_contains(t, nb, key, b2);
 }
 
 __device__ __forceinline__ void w_clear(uint32_t* t, uint32_t slots, int lane) {
@@ -318,9 +356,10 @@ __device__ __forceinline__ void stable_shift(uint32_t* bidx, float* bdist, float
     }
 }
 
-// Fix-up storage inside the slice's split area (the full replay, which uses
-// split[], only runs when the fix-ups do not fit).
-constexpr int kMaxFixSegments = 8;
+// Fix-up list in the slice's stage and eslot bytes, which the merge does not
+// otherwise use (more flagged segments than it holds take the full replay).
+constexpr int kMaxFixSegments = 4;
+constexpr int kFixBytes = 2 * 32 * 4;  // stage, eslot
 struct FixArea {
     uint32_t* mask;  // segment flags, (BLOCK_SIZE + 32) / 32 words
     uint32_t* list;  // flagged segment ids
@@ -328,24 +367,23 @@ struct FixArea {
     float* dist;
     uint16_t* at;    // output position, 0xFFFF = unused
 };
-__device__ __forceinline__ FixArea fix_area(const WSlice& s) {
-    unsigned char* b = reinterpret_cast<unsigned char*>(s.split);
+__device__ __forceinline__ FixArea fix_area(unsigned char* b) {
     FixArea f;
     f.mask = reinterpret_cast<uint32_t*>(b);
-    f.list = reinterpret_cast<uint32_t*>(b + 64);
-    f.idx = reinterpret_cast<uint32_t*>(b + 128);
-    f.dist = reinterpret_cast<float*>(b + 128 + 4 * 4 * kMaxFixSegments);
-    f.at = reinterpret_cast<uint16_t*>(b + 128 + 8 * 4 * kMaxFixSegments);
+    f.list = reinterpret_cast<uint32_t*>(b + 48);
+    f.idx = reinterpret_cast<uint32_t*>(b + 64);
+    f.dist = reinterpret_cast<float*>(b + 64 + 4 * 4 * kMaxFixSegments);
+    f.at = reinterpret_cast<uint16_t*>(b + 64 + 8 * 4 * kMaxFixSegments);
     return f;
 }
-static_assert((BLOCK_SIZE + 32) / 32 <= 16 && kMaxFixSegments <= 16, "flags and ids fit in 64 bytes each");
-static_assert(128 + 10 * 4 * kMaxFixSegments <= (BLOCK_SIZE + 1) * 2, "fix-ups fit in the split area");
+static_assert((BLOCK_SIZE + 32) / 32 <= 12 && kMaxFixSegments <= 4, "flags fit in 48 bytes, ids in 16");
+static_assert(64 + 10 * 4 * kMaxFixSegments <= kFixBytes, "fix-ups fit in stage and eslot");
 
 __device__ __noinline__ int tie_fixups(uint32_t* s_bidx, float* s_bdist, uint32_t* s_cidx, float* s_cdist,
-                                       uint32_t* s_pos, uint16_t* s_split, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
-                                       uint32_t p0, uint32_t lb, uint32_t ub, bool tie, int lane);
+                                       uint32_t* s_pos, unsigned char* s_fix, uint32_t cbs, uint32_t P, int active,
+                                       const uint16_t* bnd, uint32_t p0, uint32_t lb, uint32_t ub, bool tie, int lane);
 __device__ __noinline__ void merge_path_ties(uint32_t* s_bidx, float* s_bdist, uint32_t* s_cidx, float* s_cdist,
-                                             uint32_t* s_pos, uint16_t* s_split, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+                                             uint32_t* s_pos, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
                                              uint32_t p0, int lane);
 
 // Merge of the candidate buffer (cidx/cdist[0..cbs)) into the beam
@@ -383,15 +421,16 @@ __device__ __forceinline__ uint32_t merge_path_warp(const WSlice& s, uint32_t cb
     if (__ballot_sync(kFull, tie) != 0) {
         if (valid) s.pos[lane] = pos;
         __syncwarp();
-        nfix = tie_fixups(s.bidx, s.bdist, s.cidx, s.cdist, s.pos, s.split, cbs, P, active, bnd, p0, lb, ub, tie, lane);
+        nfix = tie_fixups(s.bidx, s.bdist, s.cidx, s.cdist, s.pos, reinterpret_cast<unsigned char*>(s.stage), cbs, P,
+                          active, bnd, p0, lb, ub, tie, lane);
         if (nfix < 0) {
-            merge_path_ties(s.bidx, s.bdist, s.cidx, s.cdist, s.pos, s.split, cbs, P, active, bnd, p0, lane);
+            merge_path_ties(s.bidx, s.bdist, s.cidx, s.cdist, s.pos, cbs, P, active, bnd, p0, lane);
             return p0;
         }
     }
     stable_shift(bidx, bdist, k, v, pos, P, p0, lane);
     if (nfix > 0) {
-        const FixArea f = fix_area(s);
+        const FixArea f = fix_area(reinterpret_cast<unsigned char*>(s.stage));
         if (lane < 4 * nfix && f.at[lane] != 0xFFFFu) {
             bidx[f.at[lane]] = f.idx[lane];
             bdist[f.at[lane]] = f.dist[lane];
@@ -417,17 +456,16 @@ __device__ __forceinline__ int count_lt(const uint32_t* a, int n, uint32_t x) {
 // fix-up list.  Returns the number of flagged segments, or -1 if they do not
 // fit the list.
 __device__ __noinline__ int tie_fixups(uint32_t* s_bidx, float* s_bdist, uint32_t* s_cidx, float* s_cdist,
-                                       uint32_t* s_pos, uint16_t* s_split, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
-                                       uint32_t p0, uint32_t lb, uint32_t ub, bool tie, int lane) {
+                                       uint32_t* s_pos, unsigned char* s_fix, uint32_t cbs, uint32_t P, int active,
+                                       const uint16_t* bnd, uint32_t p0, uint32_t lb, uint32_t ub, bool tie, int lane) {
     WSlice s;
     s.bidx = s_bidx;
     s.bdist = s_bdist;
     s.cidx = s_cidx;
     s.cdist = s_cdist;
     s.pos = s_pos;
-    s.split = s_split;
     if (P > 4u * static_cast<uint32_t>(active)) return -1;  // segments longer than the list's 4 outputs
-    const FixArea f = fix_area(s);
+    const FixArea f = fix_area(s_fix);
     constexpr int kWords = (BLOCK_SIZE + 32) / 32;
     if (lane < kWords) f.mask[lane] = 0;
     __syncwarp();
@@ -498,34 +536,18 @@ __device__ __noinline__ int tie_fixups(uint32_t* s_bidx, float* s_bdist, uint32_
     return total;
 }
 
-// A candidate ties a beam entry: the reference's split at every segment
-// boundary (split_at runs its binary search where the split is ambiguous),
-// computed before the beam is overwritten, then each output position replays
-// its segment's beam-first merge; positions are rewritten from the end and
-// every source index is <= its output.
+// More flagged segments than the fix-up list holds: every output position
+// from p0 on replays its segment's beam-first merge between the reference's
+// splits at the segment's two boundaries (split_at, which runs the
+// reference's binary search where the split is ambiguous), all computed from
+// the unmodified beam; positions are rewritten from the end and every source
+// index is <= its output.
 __device__ __noinline__ void merge_path_ties(uint32_t* s_bidx, float* s_bdist, uint32_t* s_cidx, float* s_cdist,
-                                             uint32_t* s_pos, uint16_t* s_split, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
+                                             uint32_t* s_pos, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
                                              uint32_t p0, int lane) {
-    WSlice s;
-    s.bidx = s_bidx;
-    s.bdist = s_bdist;
-    s.cidx = s_cidx;
-    s.cdist = s_cdist;
-    s.pos = s_pos;
-    s.split = s_split;
-    uint32_t* bidx = s.bidx;
-    float* bdist = s.bdist;
+    uint32_t* bidx = s_bidx;
+    float* bdist = s_bdist;
     const uint32_t first_chunk = p0 & ~31u;
-    for (int s0 = 0; s0 <= active; s0 += 32) {
-        const int sg = s0 + lane;
-        if (sg <= active) {
-            const int d = bnd[sg];
-            s.split[sg] = static_cast<uint16_t>(
-                d <= static_cast<int>(p0) ? d
-                                          : split_at(d, p0, s.pos, bdist, static_cast<int>(P), s.cdist, static_cast<int>(cbs)));
-        }
-    }
-    __syncwarp();
     for (int c0 = static_cast<int>((P - 1) & ~31u); c0 >= static_cast<int>(first_chunk); c0 -= 32) {
         const uint32_t o = static_cast<uint32_t>(c0) + lane;
         const bool act = o < P && o >= p0;
@@ -535,19 +557,19 @@ __device__ __noinline__ void merge_path_ties(uint32_t* s_bidx, float* s_bdist, u
             uint32_t sg = (o * static_cast<uint32_t>(active)) / P;  // o * active < 2^18
             if (bnd[sg + 1] <= o) ++sg;
             const int ob = bnd[sg], oe = bnd[sg + 1];
-            int ti = s.split[sg];
-            const int te = s.split[sg + 1];
+            int ti = split_at(ob, p0, s_pos, bdist, static_cast<int>(P), s_cdist, static_cast<int>(cbs));
+            const int te = split_at(oe, p0, s_pos, bdist, static_cast<int>(P), s_cdist, static_cast<int>(cbs));
             int ci = ob - ti;
             const int ce = oe - te;
             for (int j = ob;; ++j) {
-                const bool take = (ci >= ce) || (ti < te && bdist[ti] <= s.cdist[ci]);
+                const bool take = (ci >= ce) || (ti < te && bdist[ti] <= s_cdist[ci]);
                 if (j == static_cast<int>(o)) {
                     if (take) {
                         od = bdist[ti];
                         ov = bidx[ti];
                     } else {
-                        od = s.cdist[ci];
-                        ov = s.cidx[ci];
+                        od = s_cdist[ci];
+                        ov = s_cidx[ci];
                     }
                     break;
                 }
@@ -577,7 +599,7 @@ template <int W, int MERGE, bool IP>
 __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& pl, const WSlice& s,
                                              const uint16_t* bnd, uint32_t qid, bool vec, int lane) {
     constexpr bool mp = MERGE == 0;
-    constexpr int G = W <= 4 ? 16 : 8;  // rows per exact-distance round
+    constexpr int G = 8;  // rows per exact-distance round
     const int dim = a.dim, deg = a.degree, beam = a.beam;
     const uint32_t P = pl.padded, cbs = pl.cbs, slots = pl.slots;
     const float* __restrict__ rows = a.rows;
@@ -869,8 +891,8 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
     __syncwarp();
 }
 
-template <int W, int MERGE, bool IP>
-__global__ void __launch_bounds__(kWarpsPerCta * 32, kMinCtas) search_warp_kernel(const SearchArgs a, const WPlan pl,
+template <int W, int MERGE, bool IP, int MINB>
+__global__ void __launch_bounds__(kWarpsPerCta * 32, MINB) search_warp_kernel(const SearchArgs a, const WPlan pl,
                                                                                   int vec_codes) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     // merge-path output segment boundaries s * itopk / active (launch constants)
@@ -892,28 +914,31 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, kMinCtas) search_warp_kerne
     }
 }
 
-template <int W, bool IP>
+template <int W, bool IP, int MINB>
 const void* pick_merge_w(int merge) {
     switch (merge) {
-        case 1: return reinterpret_cast<const void*>(search_warp_kernel<W, 1, IP>);
-        case 2: return reinterpret_cast<const void*>(search_warp_kernel<W, 2, IP>);
-        case 4: return reinterpret_cast<const void*>(search_warp_kernel<W, 4, IP>);
-        default: return reinterpret_cast<const void*>(search_warp_kernel<W, 0, IP>);
+        case 1: return reinterpret_cast<const void*>(search_warp_kernel<W, 1, IP, MINB>);
+        case 2: return reinterpret_cast<const void*>(search_warp_kernel<W, 2, IP, MINB>);
+        case 4: return reinterpret_cast<const void*>(search_warp_kernel<W, 4, IP, MINB>);
+        default: return reinterpret_cast<const void*>(search_warp_kernel<W, 0, IP, MINB>);
     }
 }
 
-template <bool IP>
+template <bool IP, int MINB>
 const void* pick_w(int W, int merge) {
     switch (W) {
-        case 1: return pick_merge_w<1, IP>(merge);
-        case 2: return pick_merge_w<2, IP>(merge);
-        case 4: return pick_merge_w<4, IP>(merge);
-        default: return pick_merge_w<8, IP>(merge);
+        case 1: return pick_merge_w<1, IP, MINB>(merge);
+        case 2: return pick_merge_w<2, IP, MINB>(merge);
+        case 4: return pick_merge_w<4, IP, MINB>(merge);
+        default: return pick_merge_w<8, IP, MINB>(merge);
     }
 }
 
-// kernel for W = padded dim / 32, the beam merge and the metric
-const void* warp_kernel_for(int W, int merge, bool ip) { return ip ? pick_w<true>(W, merge) : pick_w<false>(W, merge); }
+// kernel for W = padded dim / 32, the beam merge, the metric and the register budget
+const void* warp_kernel_for(int W, int merge, bool ip, int minb) {
+    if (minb == kCtasSmall) return ip ? pick_w<true, kCtasSmall>(W, merge) : pick_w<false, kCtasSmall>(W, merge);
+    return ip ? pick_w<true, kCtasLarge>(W, merge) : pick_w<false, kCtasLarge>(W, merge);
+}
 
 }  // namespace
 
@@ -922,7 +947,7 @@ bool warp_kernel_supports(int padded_dim) { return padded_dim >= 32 && padded_di
 int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, size_t errlen) {
     const int D = a.padded_dim;
     uint32_t req = p->padded + p->cbs * SMALL_HASH_RESET_INTERVAL;
-    uint32_t slots = (req * 4 + 2) / 3;
+    uint32_t slots = req + (req + 11) / 12;  // ~93 % at the bound (two-choice buckets)
     // the table doubles as the query's scratch during set-up
     const uint32_t scratch = (static_cast<uint32_t>((a.dim + 3) & ~3) * 4 + static_cast<uint32_t>(D) + 3) / 4;
     if (slots < scratch) slots = scratch;
@@ -932,9 +957,11 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
     p->slice_bytes = slice_layout(p->padded, slots, D, p->merge_n2 == 0, nullptr, nullptr);
     p->smem_bytes = p->slice_bytes * kWarpsPerCta;
     p->threads = kWarpsPerCta * 32;
-    int sms = 0, max_smem = 0;
+    int sms = 0, max_smem = 0, sm_smem = 0, reserved = 0;
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, device);
     if (e != cudaSuccess) {
         snprintf(err, errlen, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
         return FG_ERR_CUDA;
@@ -943,7 +970,10 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
         snprintf(err, errlen, "shared memory %zu exceeds the device limit %d", p->smem_bytes, max_smem);
         return FG_ERR_UNSUPPORTED;
     }
-    const void* fn = warp_kernel_for(D / 32, p->merge_n2, a.use_ip != 0);
+    // the smaller register budget only where a fifth CTA's slices fit the SM
+    const size_t per_cta = p->smem_bytes + static_cast<size_t>(reserved);
+    p->min_ctas = static_cast<size_t>(kCtasSmall) * per_cta <= static_cast<size_t>(sm_smem) ? kCtasSmall : kCtasLarge;
+    const void* fn = warp_kernel_for(D / 32, p->merge_n2, a.use_ip != 0, p->min_ctas);
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p->smem_bytes));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
@@ -977,7 +1007,7 @@ cudaError_t launch_search_warp(const SearchArgs& a, const SearchPlan& p, cudaStr
     pl.slice = static_cast<uint32_t>(p.slice_bytes);
     cudaError_t e = cudaMemsetAsync(a.work_counter, 0, sizeof(uint32_t), stream);
     if (e != cudaSuccess) return e;
-    const void* fn = warp_kernel_for(a.padded_dim / 32, p.merge_n2, a.use_ip != 0);
+    const void* fn = warp_kernel_for(a.padded_dim / 32, p.merge_n2, a.use_ip != 0, p.min_ctas);
     SearchArgs args = a;
     int vec = p.vec_codes;
     void* params[] = {&args, &pl, &vec};
