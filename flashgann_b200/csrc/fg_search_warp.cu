@@ -5,7 +5,7 @@
 // for throughput instead of per-query latency: each warp of a CTA is an
 // independent worker that pulls query ids from the global counter and runs
 // the whole iteration on its own, with no block barrier anywhere.  A CTA
-// holds kWarpsPerCta queries; the per-warp state (beam, visited set, bit
+// holds up to kWarpsPerCta queries; the per-warp state (beam, visited set, bit
 // planes, candidate buffer) is a private slice of shared memory.
 //
 // Per iteration the warp
@@ -44,7 +44,7 @@ static_assert(SEARCH_WIDTH <= 32, "expanders are picked by one warp");
 namespace fg {
 namespace {
 
-constexpr int kWarpsPerCta = 4;
+constexpr int kWarpsPerCta = 4;  // largest CTA; the planner may launch 1 or 2 warps per CTA
 // Register budgets: 4 CTAs per SM (128 registers per thread) or, when the
 // query slices of 5 CTAs fit the SM's shared memory, 5 (96 registers).
 constexpr int kCtasLarge = 4;
@@ -898,7 +898,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, MINB) search_warp_kernel(co
     // merge-path output segment boundaries s * itopk / active (launch constants)
     __shared__ uint16_t bnd[MERGE == 0 ? BLOCK_SIZE + 1 : 1];
     if constexpr (MERGE == 0) {
-        for (int sg = threadIdx.x; sg <= pl.mp_active; sg += kWarpsPerCta * 32)
+        for (int sg = threadIdx.x; sg <= pl.mp_active; sg += blockDim.x)
             bnd[sg] = static_cast<uint16_t>((static_cast<uint32_t>(sg) * pl.padded) / static_cast<uint32_t>(pl.mp_active));
     }
     __syncthreads();  // the only block barrier: the warps are independent from here on
@@ -955,41 +955,58 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
     p->kernel = 1;
     p->slots = slots;
     p->slice_bytes = slice_layout(p->padded, slots, D, p->merge_n2 == 0, nullptr, nullptr);
-    p->smem_bytes = p->slice_bytes * kWarpsPerCta;
-    p->threads = kWarpsPerCta * 32;
-    int sms = 0, max_smem = 0, sm_smem = 0, reserved = 0;
+    int sms = 0, max_smem = 0;
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, device);
     if (e != cudaSuccess) {
         snprintf(err, errlen, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
         return FG_ERR_CUDA;
     }
-    if (p->smem_bytes > static_cast<size_t>(max_smem)) {
-        snprintf(err, errlen, "shared memory %zu exceeds the device limit %d", p->smem_bytes, max_smem);
+    if (p->slice_bytes > static_cast<size_t>(max_smem)) {
+        snprintf(err, errlen, "shared memory %zu exceeds the device limit %d", p->slice_bytes, max_smem);
         return FG_ERR_UNSUPPORTED;
     }
-    // the smaller register budget only where a fifth CTA's slices fit the SM
-    const size_t per_cta = p->smem_bytes + static_cast<size_t>(reserved);
-    p->min_ctas = static_cast<size_t>(kCtasSmall) * per_cta <= static_cast<size_t>(sm_smem) ? kCtasSmall : kCtasLarge;
-    const void* fn = warp_kernel_for(D / 32, p->merge_n2, a.use_ip != 0, p->min_ctas);
-    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p->smem_bytes));
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    // resident queries per SM for every register budget and CTA size (queries
+    // per CTA), as the occupancy calculator counts them; the most wins, ties
+    // go to the larger CTA
+    const void* best = nullptr;
+    int best_q = 0;
+    for (int minb : {kCtasSmall, kCtasLarge}) {
+        const void* fn = warp_kernel_for(D / 32, p->merge_n2, a.use_ip != 0, minb);
+        for (int wpc : {kWarpsPerCta, 2, 1}) {
+            const size_t smem = p->slice_bytes * static_cast<size_t>(wpc);
+            if (smem > static_cast<size_t>(max_smem)) continue;
+            e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+            int per_sm = 0;
+            if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, wpc * 32, smem);
+            if (e != cudaSuccess) {
+                snprintf(err, errlen, "occupancy query failed: %s", cudaGetErrorString(e));
+                return FG_ERR_CUDA;
+            }
+            if (per_sm * wpc > best_q) {
+                best_q = per_sm * wpc;
+                best = fn;
+                p->min_ctas = minb;
+                p->threads = wpc * 32;
+                p->smem_bytes = smem;
+                p->blocks_per_sm = per_sm;
+            }
+        }
+    }
+    if (!best) {
+        snprintf(err, errlen, "no launch shape fits: %zu bytes of shared memory per query", p->slice_bytes);
+        return FG_ERR_UNSUPPORTED;
+    }
+    e = cudaFuncSetAttribute(best, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p->smem_bytes));
     if (e != cudaSuccess) {
         snprintf(err, errlen, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         return FG_ERR_CUDA;
     }
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, p->threads, p->smem_bytes);
-    if (e != cudaSuccess || per_sm < 1) {
-        snprintf(err, errlen, "occupancy query failed: %s", cudaGetErrorString(e));
-        return FG_ERR_CUDA;
-    }
-    p->blocks_per_sm = per_sm;
-    const int resident = per_sm * sms;
-    const int need = (a.nq + kWarpsPerCta - 1) / kWarpsPerCta;
+    const int wpc = p->threads / 32;
+    const int resident = p->blocks_per_sm * sms;
+    const int need = (a.nq + wpc - 1) / wpc;
     p->grid = need < resident ? need : resident;
     if (p->grid < 1) p->grid = 1;
     return FG_OK;
