@@ -107,3 +107,23 @@ def test_ground_truth_is_exact():
     for i in range(8):
         order = np.lexsort((np.arange(ds.spec.n), d[i]))[: ds.gt.shape[1]]
         assert np.array_equal(order, ds.gt[i])
+
+
+def test_shards_partition_the_base_with_local_graphs(tmp_path):
+    from flashgann_b200 import builder
+    spec = builder.SPECS["t_2k"]
+    full = builder.materialize(spec, cache_dir=str(tmp_path))
+    L = full.layout
+    seen = 0
+    for i in range(3):
+        sh = builder.materialize_shard(spec, i, 3, cache_dir=str(tmp_path))
+        s, e = builder.shard_range(spec.n, 3, i)
+        assert (sh.offset, sh.n) == (s, e - s) and s == seen
+        seen = e
+        assert np.array_equal(sh.rows[:, :spec.dim], full.base[s:e])
+        ids = sh.rows.view(np.uint32)[:, L.nbr_off:L.nbr_off + L.degree]
+        assert ((ids < sh.n) | (ids == 0xFFFFFFFF)).all()
+        assert 0 <= sh.entry < sh.n
+        assert np.array_equal(sh.signs, full.signs)
+        assert np.array_equal(sh.gt, full.gt)
+    assert seen == spec.n
