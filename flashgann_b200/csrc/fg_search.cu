@@ -729,10 +729,17 @@ int variant_from_env() {
     return (x >= 0 && x < kNumVariants) ? x : kDefaultVariant;
 }
 
-// FG_KERNEL=cta selects the CTA-per-query kernel where the warp kernel applies.
-bool cta_kernel_forced() {
+// Kernel choice where both apply (padded dim <= 256; they return identical
+// results): the warp kernel for batches of more than 4 queries per SM, where
+// its 20 resident queries per SM pay; below that the CTA kernel's 8 warps per
+// query finish sooner.  FG_KERNEL=warp or FG_KERNEL=cta forces one.
+bool use_warp_kernel(int nq, int device) {
     const char* v = getenv("FG_KERNEL");
-    return v && v[0] == 'c';
+    if (v && v[0] == 'c') return false;
+    if (v && v[0] == 'w') return true;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) sms = 148;
+    return nq > 4 * sms;
 }
 
 int merge_width(uint32_t itopk) {
@@ -806,7 +813,7 @@ int plan_search(const SearchArgs& a, SearchPlan* p, int device, char* err, size_
     p->mp_active = merge_active(p->padded);
     const uintptr_t base = reinterpret_cast<uintptr_t>(a.rows);
     p->vec_codes = ((base % 16) == 0 && ((a.row * 4) % 16) == 0 && ((a.code_off * 4) % 16) == 0) ? 1 : 0;
-    if (warp_kernel_supports(a.padded_dim) && !cta_kernel_forced()) return plan_search_warp(a, p, device, err, errlen);
+    if (warp_kernel_supports(a.padded_dim) && use_warp_kernel(a.nq, device)) return plan_search_warp(a, p, device, err, errlen);
     p->kernel = 0;
     p->variant = variant_from_env();
     const int nw = kVariants[p->variant].nw;

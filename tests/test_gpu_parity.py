@@ -49,8 +49,15 @@ def _run_gpu(qg, queries, K, beam, trace_cap=0):
     return out
 
 
+@pytest.fixture(params=["warp", "cta"])
+def kernel(request, monkeypatch):
+    """Both search kernels (the planner picks by batch size; FG_KERNEL forces one)."""
+    monkeypatch.setenv("FG_KERNEL", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("name,beams", CASES)
-def test_search_matches_oracle(name, beams):
+def test_search_matches_oracle(name, beams, kernel):
     ds, qg = _gpu_index(name)
     oi = oracle_index(name)
     K = ds.spec.K
@@ -81,7 +88,7 @@ def test_search_matches_oracle(name, beams):
 
 
 @pytest.mark.parametrize("name,beams", [("t_4k96f", (64, 100, 256)), ("t_2k", (128, 200))])
-def test_inner_product_search_matches_oracle(name, beams):
+def test_inner_product_search_matches_oracle(name, beams, kernel):
     """METRIC_IP (the reference's Text2Image path, negated dot products) on a
     normalised 96-d set (padded to D = 128) and an integer 128-d set."""
     import oracle
