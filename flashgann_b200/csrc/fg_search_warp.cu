@@ -5,28 +5,32 @@
 // for throughput instead of per-query latency: each warp of a CTA is an
 // independent worker that pulls query ids from the global counter and runs
 // the whole iteration on its own, with no block barrier anywhere.  A CTA
-// holds up to kWarpsPerCta queries; the per-warp state (beam, visited set, bit
-// planes, candidate buffer) is a private slice of shared memory.
+// holds 1, 2 or 4 queries (the planner picks the shape with the most resident
+// queries per SM); the per-warp state (beam, visited set, bit planes,
+// candidate buffer) is a private slice of shared memory.
 //
 // Per iteration the warp
 //   * merges the pending candidates into the beam in place: candidate m lands
 //     at pos[m] = m + #{beam <= cand[m]} (the stable, beam-first merge), and
 //     the beam tail is shifted chunk by chunk from the end.  The reference's
 //     merge path differs from the stable merge only where a beam entry and a
-//     candidate have equal distances at one of its segment boundaries; when a
-//     candidate ties the beam the warp computes the reference's split at every
-//     segment boundary first and replays its per-segment merge;
+//     candidate have equal distances at one of its segment boundaries: the
+//     segments next to such a boundary are replayed with the reference's
+//     splits before the shift and written over it (a full replay covers more
+//     than the fix-up list holds);
 //   * picks the expanders and runs the adaptive controller (warp-uniform
 //     registers);
-//   * expands: lane l holds neighbour l of every parent (ids, factors and
-//     packed codes loaded for all parents before any is examined), visited
-//     lookups, bit-plane RaBitQ estimates and the keep rule per parent;
+//   * expands one parent per step, lane l holding neighbour l, while the next
+//     parent's block loads: visited lookups (all before any insert of the
+//     iteration), bit-plane RaBitQ estimates and the keep rule;
 //   * compacts the kept children (first parent wins a shared child) with
 //     __match_any_sync, inserts them into the visited set and computes their
 //     exact distances G rows at a time: every lane accumulates its strided
 //     dimensions of each row in the reference's order, then the reference's
 //     shuffle tree runs transposed (lanes split the rows), which gives the
 //     same sums with G-1+log2(32/G) shuffles instead of 5 per row.
+// The visited set is exact and two-choice (see w_insert), which keeps it
+// small enough for 5 CTAs of 4 queries per SM up to beam 640 at D = 128.
 #include <cfloat>
 #include <cstdint>
 #include <cstdio>
