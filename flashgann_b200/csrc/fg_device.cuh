@@ -1,5 +1,6 @@
-// fg_device.cuh -- device building blocks of the search (included by
-// fg_search.cu only): the warp bitonic network, the visited set, query
+// fg_device.cuh -- device building blocks of the search (included by both
+// kernels, fg_search.cu and fg_search_warp.cu): the warp bitonic network, the
+// CTA kernel's visited set, query
 // rotation/quantisation, bit-plane RaBitQ estimates, exact distances, the
 // adaptive controller and both beam merges.
 //
@@ -491,23 +492,6 @@ __device__ __forceinline__ float warp_dist(const float* __restrict__ r, const fl
 // ----------------------------------------------------- adaptive controller
 // src/adaptive_search_utils.cuh:8-135 and the call site at
 // src/adaptive_search.cuh:166-217.
-struct Ctl {
-    int theta;
-    float rho;
-    int policy_iters;
-    uint32_t top1;
-    int stall;
-    int warmup_done;
-    float entry_d, last_d, cur_d;
-    uint32_t keep_exp;
-    float cutoff;
-    uint32_t scan_start;
-    uint32_t merge_p0;
-    uint32_t n_eval;
-    uint32_t n_est;
-    uint32_t query;
-};
-
 __device__ __forceinline__ bool finite_lt_max(float x) { return isfinite(x) && x < FLT_MAX; }
 
 __device__ __forceinline__ int clamp_i(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
@@ -542,40 +526,6 @@ __device__ __forceinline__ int keep_for(uint32_t active, int theta, float rho, b
     int mk = rho_keep < budget ? rho_keep : budget;
     if (cut_valid) mk = clamp_i(static_cast<int>(near), 1, mk);
     return clamp_i(mk, 1, ac);
-}
-
-__device__ void controller_step(Ctl& c, uint32_t beam0, int iter, float phase2_rho) {
-    const uint32_t top1 = beam0 & 0x7fffffffu;
-    const int stall = (c.policy_iters > 0 && top1 == c.top1) ? c.stall + 1 : 0;
-    const bool changed = c.warmup_done || stall >= TOP1_WARMUP_STALL_ITERS;
-    // update_expander_progress
-    const float e = c.entry_d;
-    const float last = finite_lt_max(c.last_d) ? c.last_d : e;
-    const float cur = finite_lt_max(c.cur_d) ? c.cur_d : last;
-    float rate = 0.0f;
-    const float denom = fabsf(e);
-    if (isfinite(last) && isfinite(cur) && isfinite(e) && !(denom <= 1.0e-20f)) {
-        const float prog = __fdiv_rn(__fsub_rn(last, cur), denom);
-        if (isfinite(prog) && prog > 0.0f) rate = prog < 1.0f ? prog : 1.0f;
-    }
-    c.top1 = top1;
-    c.stall = stall;
-    c.last_d = last;
-    c.cur_d = cur;
-    if (changed) {
-        c.warmup_done = 1;
-        c.theta = PHASE2_THETA;
-        c.rho = phase2_rho;
-        c.policy_iters += 1;
-    } else if (iter == 0 || (iter % CHECK_INTERVAL) == 0) {
-        const float span = phase2_rho > PHASE1_RHO ? __fsub_rn(phase2_rho, PHASE1_RHO) : __fsub_rn(RHO_MAX, RHO_MIN);
-        const float base = c.policy_iters == 0 ? PHASE1_RHO : c.rho;
-        const float cap = phase2_rho > PHASE1_RHO ? phase2_rho : RHO_MAX;
-        c.warmup_done = 0;
-        c.theta = PHASE1_THETA;
-        c.rho = clamp_f(__fmaf_rn(span, rate, base), RHO_MIN, cap);
-        c.policy_iters += 1;
-    }
 }
 
 // smallest `eff` valid lanes by (estimate, lane) -- the rank rule of

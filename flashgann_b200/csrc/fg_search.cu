@@ -1,4 +1,6 @@
-// fg_search.cu -- the B200 search kernel and its launcher.
+// fg_search.cu -- the one-CTA-per-query search kernel, the planner and the
+// launchers (the planner hands batches of more than 4 queries per SM with a
+// padded dimension <= 256 to the warp-per-query kernel, fg_search_warp.cu).
 //
 // One persistent kernel runs the reference's whole per-query search
 // (SophiaSun18/FlashGANN src/adaptive_search.cuh:5-466): each CTA of NW warps
