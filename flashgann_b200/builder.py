@@ -97,7 +97,7 @@ class DatasetSpec:
     K: int
     beams: Tuple[int, ...]
     seed: int
-    kind: str = "int_gmm"      # int_gmm | norm_aniso | lowrank
+    kind: str = "int_gmm"      # int_gmm | int_gmm_dup | norm_aniso | lowrank
     knn_k: int = 64
     gt_k: int = 100
 
@@ -125,6 +125,9 @@ SPECS = {
                            (100, 256), seed=13, kind="norm_aniso"),
     "t_2k": DatasetSpec("t_2k", 2_000, 64, 128, 4, 25.0, 0.0, 255.0, 32, 100,
                         (32, 100, 128, 200, 256), seed=14),
+    # every vector four times: equal distances everywhere (tie paths of the merges)
+    "t_2kdup": DatasetSpec("t_2kdup", 2_000, 64, 128, 4, 25.0, 0.0, 255.0, 32, 100,
+                           (100, 200, 256, 512), seed=17, kind="int_gmm_dup"),
     # padded dimensions above 256 (the one-CTA-per-query kernel): 300 -> 512, 1536 -> 2048
     "t_2k300": DatasetSpec("t_2k300", 2_000, 48, 300, 4, 25.0, 0.0, 255.0, 32, 100,
                            (100, 256), seed=15),
@@ -171,6 +174,12 @@ def generate_vectors(spec: DatasetSpec) -> Tuple[np.ndarray, np.ndarray]:
             return v.astype(np.float32)
 
         return draw(1, spec.n), draw(2, spec.nq)
+    if spec.kind == "int_gmm_dup":
+        # every base vector repeated 4 times (consecutive ids): long runs of
+        # equal distances, for the merges' tie paths
+        uniq = dataclasses.replace(spec, n=(spec.n + 3) // 4, kind="int_gmm")
+        base, queries = generate_vectors(uniq)
+        return np.repeat(base, 4, axis=0)[:spec.n].copy(), queries
     if spec.kind == "lowrank":
         # rank-64 latent x a fixed 64 x dim map + N(0, 0.02^2), L2-normalised
         cr = _rng(spec.seed, 0)

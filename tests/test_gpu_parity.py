@@ -15,6 +15,8 @@ CASES = [
     ("t_2k", (32, 100, 128, 200, 256)),
     ("t_8k16", (16, 32, 64, 96, 128, 256, 512)),
     ("t_20k", (100, 128, 256, 384, 512, 1024)),
+    # every vector four times: long runs of equal distances through both merges' tie paths
+    ("t_2kdup", (100, 128, 200, 256, 512)),
     # padded dimension 512 and 2048: the one-CTA-per-query kernel
     ("t_2k300", (100, 256)),
     ("t_1k1536", (32, 128)),
