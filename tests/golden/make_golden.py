@@ -11,9 +11,12 @@ Writes, under --out:
                      adaptive rho / keep-count update
   ref_search_<ds>.npz  result ids of QuantizationGraph::gpu_search_adaptive
                      for every beam of a seeded dataset, two runs each
+                     (<ds>_ip: with the inner-product metric, set_metric(IP))
   manifest.json      dataset digests and shapes
 
 Usage:  python tests/golden/make_golden.py --out gpurun_out/golden
+        python tests/golden/make_golden.py --out gpurun_out/golden --no-unit \
+            --sets t_2kdup,t_2k:ip --manifest-in tests/golden/manifest.json
 """
 
 from __future__ import annotations
@@ -32,7 +35,7 @@ sys.path.insert(0, ROOT)
 from flashgann_b200 import builder  # noqa: E402
 from oracle import ref  # noqa: E402
 
-SEARCH_SETS = ["t_2k", "t_8k16", "t_20k", "c1_100k"]
+SEARCH_SETS = ["t_2k", "t_8k16", "t_20k", "c1_100k", "t_2kdup", "t_2k:ip"]
 
 
 def unit_goldens(rng: np.random.Generator):
@@ -160,13 +163,17 @@ def unit_goldens(rng: np.random.Generator):
     return out
 
 
-def search_goldens(name: str, manifest: dict, out_dir: str, device: str) -> None:
+def search_goldens(entry: str, manifest: dict, out_dir: str, device: str) -> None:
     t0 = time.time()
+    name, _, metric = entry.partition(":")
+    ip = metric == "ip"
+    key = f"{name}_ip" if ip else name
     ds = builder.materialize(name, device=device)
     spec = ds.spec
-    manifest[name] = dict(digest=ds.digest(), n=spec.n, dim=spec.dim, degree=spec.degree, K=spec.K,
-                          beams=list(spec.beams), nq=spec.nq, entry=int(ds.entry))
-    g = ref.RefGraph(ds.codebook_path, spec.n, spec.dim, spec.degree)
+    manifest[key] = dict(digest=ds.digest(), n=spec.n, dim=spec.dim, degree=spec.degree, K=spec.K,
+                         beams=list(spec.beams), nq=spec.nq, entry=int(ds.entry), dataset=name,
+                         metric="ip" if ip else "l2")
+    g = ref.RefGraph(ds.codebook_path, spec.n, spec.dim, spec.degree, use_ip=ip)
     res = {}
     for beam in spec.beams:
         a, _ = g.search(ds.queries, spec.K, beam)
@@ -174,10 +181,10 @@ def search_goldens(name: str, manifest: dict, out_dir: str, device: str) -> None
         res[f"ids_{beam}"] = a
         res[f"ids2_{beam}"] = b
         diff = int((a != b).any(axis=1).sum())
-        manifest[name][f"run_to_run_queries_differing_{beam}"] = diff
+        manifest[key][f"run_to_run_queries_differing_{beam}"] = diff
     g.close()
-    np.savez_compressed(os.path.join(out_dir, f"ref_search_{name}.npz"), **res)
-    print(f"[golden] {name}: {time.time() - t0:.1f}s", flush=True)
+    np.savez_compressed(os.path.join(out_dir, f"ref_search_{key}.npz"), **res)
+    print(f"[golden] {key}: {time.time() - t0:.1f}s", flush=True)
 
 
 def main() -> None:
@@ -185,14 +192,21 @@ def main() -> None:
     ap.add_argument("--out", default=os.path.join(ROOT, "gpurun_out", "golden"))
     ap.add_argument("--sets", default=",".join(SEARCH_SETS))
     ap.add_argument("--device", default="cuda")
+    ap.add_argument("--no-unit", action="store_true", help="skip the device-function goldens")
+    ap.add_argument("--manifest-in", default="", help="existing manifest to add the new search sets to")
     args = ap.parse_args()
     os.makedirs(args.out, exist_ok=True)
-    rng = np.random.default_rng(20260101)
-    t0 = time.time()
-    unit = unit_goldens(rng)
-    np.savez_compressed(os.path.join(args.out, "ref_unit.npz"), **unit)
-    print(f"[golden] unit: {time.time() - t0:.1f}s", flush=True)
-    manifest = dict(reference_internal_topk=int(ref.lib().ref_internal_topk()))
+    if not args.no_unit:
+        rng = np.random.default_rng(20260101)
+        t0 = time.time()
+        unit = unit_goldens(rng)
+        np.savez_compressed(os.path.join(args.out, "ref_unit.npz"), **unit)
+        print(f"[golden] unit: {time.time() - t0:.1f}s", flush=True)
+    manifest = {}
+    if args.manifest_in:
+        with open(args.manifest_in) as f:
+            manifest = json.load(f)
+    manifest["reference_internal_topk"] = int(ref.lib().ref_internal_topk())
     for name in [s for s in args.sets.split(",") if s]:
         search_goldens(name, manifest, args.out, args.device)
     with open(os.path.join(args.out, "manifest.json"), "w") as f:

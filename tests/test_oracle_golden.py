@@ -105,24 +105,29 @@ def test_controller_rho_and_keep():
         assert ko.value == int(UNIT["ct_keep_out"][i]), i
 
 
-SEARCH_SETS = ["t_2k", "t_8k16", "t_20k"]
+SEARCH_SETS = ["t_2k", "t_8k16", "t_20k", "t_2k_ip"]
 
 
-def tie_order_only(ids, want, base, query):
+def tie_order_only(ids, want, base, query, ip=False):
     """True when two result rows hold the same ids and every position where
-    they differ lies inside a run of equal exact distances."""
+    they differ lies inside a run of equal exact distances (squared L2, or
+    the negated dot product for the inner-product metric)."""
     if set(ids.tolist()) != set(want.tolist()):
         return False
-    d = ((base[ids.astype(np.int64)].astype(np.float64) - query) ** 2).sum(1)
-    dw = ((base[want.astype(np.int64)].astype(np.float64) - query) ** 2).sum(1)
-    return np.array_equal(d, dw)
+
+    def dist(rows):
+        x = base[rows.astype(np.int64)].astype(np.float64)
+        return -(x @ query) if ip else ((x - query) ** 2).sum(1)
+
+    return np.array_equal(dist(ids), dist(want))
 
 
-def compare_with_reference(ds, ids, want):
+def compare_with_reference(ds, ids, want, ip=False):
     """Queries whose ids differ from the reference beyond tie order, and the
     number that differ only in the order of equal-distance results."""
     rows = np.nonzero((ids != want).any(axis=1))[0]
-    ties = [int(i) for i in rows if tie_order_only(ids[i], want[i], ds.base, ds.queries[i].astype(np.float64))]
+    ties = [int(i) for i in rows
+            if tie_order_only(ids[i], want[i], ds.base, ds.queries[i].astype(np.float64), ip)]
     return [int(i) for i in rows if i not in ties], len(ties)
 
 
@@ -142,13 +147,49 @@ def test_search_matches_reference(name):
     if man is None or g is None:
         pytest.skip("search goldens not generated yet")
     import oracle
-    ds = dataset(name)
+    ds = dataset(man.get("dataset", name))
     assert ds.digest() == man["digest"], "regenerated dataset differs from the golden one"
-    oi = oracle.OracleIndex(ds.rows, ds.signs, ds.entry, ds.spec.dim, ds.spec.degree)
+    oi = oracle.OracleIndex(ds.rows, ds.signs, ds.entry, ds.spec.dim, ds.spec.degree,
+                            use_ip=man.get("metric") == "ip")
     for beam in man["beams"]:
         ids, _ = oi.search(ds.queries, man["K"], beam)
         want = g[f"ids_{beam}"]
-        bad, ties = compare_with_reference(ds, ids, want)
+        bad, ties = compare_with_reference(ds, ids, want, man.get("metric") == "ip")
         assert not bad, f"{name} beam {beam}: queries {bad[:10]} differ from the reference"
         assert ties <= max(1, len(ids) // 100), f"{name} beam {beam}: {ties} tie-order differences"
         assert oracle.compute_recall(ids, ds.gt, man["K"]) == oracle.compute_recall(want, ds.gt, man["K"])
+
+
+def test_duplicate_heavy_search_agrees_as_much_as_the_reference_with_itself():
+    """t_2kdup stores every vector four times.  There the reference's race
+    (several warps inserting a child kept by two parents, see above) fires in
+    most iterations, and two runs of the reference build return the same ids
+    for only 9-19 of the 64 queries and the same sorted distance list for
+    58-60 of them (tests/golden/manifest.json, run_to_run_*).  Exact pinning
+    is impossible, so this checks that the oracle's sorted distances equal
+    those of one of the two reference runs about as often as the runs agree
+    with each other, and that recall matches within 0.01."""
+    man = golden_manifest().get("t_2kdup")
+    g = golden("ref_search_t_2kdup.npz")
+    if man is None or g is None:
+        pytest.skip("search goldens not generated yet")
+    import oracle
+    ds = dataset("t_2kdup")
+    assert ds.digest() == man["digest"]
+    oi = oracle.OracleIndex(ds.rows, ds.signs, ds.entry, ds.spec.dim, ds.spec.degree)
+
+    def sorted_dists(ids, q):
+        return np.sort(((ds.base[ids.astype(np.int64)].astype(np.float64) - q) ** 2).sum(1))
+
+    for beam in man["beams"]:
+        ids, _ = oi.search(ds.queries, man["K"], beam)
+        a, b = g[f"ids_{beam}"], g[f"ids2_{beam}"]
+        ours = runs = 0
+        for i in range(len(ids)):
+            q = ds.queries[i].astype(np.float64)
+            da, db, do = sorted_dists(a[i], q), sorted_dists(b[i], q), sorted_dists(ids[i], q)
+            ours += np.array_equal(do, da) or np.array_equal(do, db)
+            runs += np.array_equal(da, db)
+        assert ours >= runs - len(ids) // 16, f"beam {beam}: {ours} vs the reference's own {runs} of {len(ids)}"
+        r = oracle.compute_recall(ids, ds.gt, man["K"])
+        assert abs(r - oracle.compute_recall(a, ds.gt, man["K"])) <= 0.01
