@@ -109,6 +109,9 @@ SPECS = {
     # the headline case
     "c2_1m": DatasetSpec("c2_1m", 1_000_000, 10_000, 128, 200, 25.0, 0.0, 255.0, 32, 100,
                          (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=2),
+    # BASELINE.json configs[2] (10M x 96, L2-normalised anisotropic mixture) at a tenth of the base size
+    "c3s_1m": DatasetSpec("c3s_1m", 1_000_000, 10_000, 96, 1000, 0.0, 0.0, 0.0, 32, 100,
+                          (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=5, kind="norm_aniso"),
     # BASELINE.json configs[3] (1M x 1536, L2-normalised low-rank) at a fifth of the base size
     "c4s_200k": DatasetSpec("c4s_200k", 200_000, 1_000, 1536, 1, 0.0, 0.0, 0.0, 32, 100,
                             (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=4, kind="lowrank"),
