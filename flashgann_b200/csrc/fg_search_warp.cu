@@ -299,6 +299,38 @@ __device__ __forceinline__ int keep_cap(uint32_t active, int theta, float rho) {
     return rho_keep < budget ? rho_keep : budget;
 }
 
+// raw_sum (fg_device.cuh) reading the bit planes and the wrap mask with
+// 128-bit shared loads (the slice keeps them 16-byte aligned; W % 4 == 0).
+template <int W>
+__device__ __forceinline__ uint32_t raw_sum_v(const uint32_t (&c)[W], const uint32_t* planes, const uint32_t* wrap,
+                                              bool wrap_any) {
+    static_assert(W % 4 == 0, "128-bit plane words");
+    const uint4* pl = reinterpret_cast<const uint4*>(planes);
+    uint32_t raw = 0;
+#pragma unroll
+    for (int p = 0; p < kPlanes; ++p) {
+        uint32_t sum = 0;
+#pragma unroll
+        for (int w = 0; w < W; w += 4) {
+            const uint4 v = pl[(p * W + w) / 4];
+            sum += __popc(c[w] & v.x) + __popc(c[w + 1] & v.y) + __popc(c[w + 2] & v.z) + __popc(c[w + 3] & v.w);
+        }
+        raw += sum << p;
+    }
+    if (wrap_any) {
+        const uint4* wr = reinterpret_cast<const uint4*>(wrap);
+#pragma unroll
+        for (int w = 0; w < W; w += 4) {
+            const uint4 v = wr[w / 4];
+            const uint32_t m[4] = {c[w] & v.x, c[w + 1] & v.y, c[w + 2] & v.z, c[w + 3] & v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                raw -= 256u * static_cast<uint32_t>(__popc(m[j] & (m[j] >> 1) & (m[j] >> 2) & (m[j] >> 3) & 0x11111111u));
+        }
+    }
+    return raw;
+}
+
 // L2 prefetch of a row's raw vector (128-byte lines).
 __device__ __forceinline__ void prefetch_row(const float* r, int dim) {
     for (int l = 0; l < dim; l += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(r + l));
@@ -831,8 +863,13 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
                     if (valid) {
                         // speculative variant: triple_x == FLT_MAX estimates FLT_MAX
                         if (cur.tx != FLT_MAX) {
-                            const float* prow = rows + static_cast<uint64_t>(s.pnode[t]) * rowf;
-                            const uint32_t raw = parent_raw<W>(cur, prow, a, lane, s.planes, s.wrap, qsl.wrap_any);
+                            uint32_t raw;
+                            if constexpr (W % 4 == 0) {
+                                raw = raw_sum_v<W>(cur.c, s.planes, s.wrap, qsl.wrap_any);
+                            } else {
+                                const float* prow = rows + static_cast<uint64_t>(s.pnode[t]) * rowf;
+                                raw = parent_raw<W>(cur, prow, a, lane, s.planes, s.wrap, qsl.wrap_any);
+                            }
                             est = estimate(raw, cur.tx, cur.fdq, cur.fvq, s.pdist[t], qsl);
                         }
                         valid = isfinite(est);
