@@ -14,9 +14,10 @@ Writes, under --out:
                      (<ds>_ip: with the inner-product metric, set_metric(IP))
   manifest.json      dataset digests and shapes
 
-Usage:  python tests/golden/make_golden.py --out gpurun_out/golden
-        python tests/golden/make_golden.py --out gpurun_out/golden --no-unit \
+Usage:  python tests/golden/make_golden.py --out golden_out
+        python tests/golden/make_golden.py --out golden_out --no-unit \
             --sets t_2kdup,t_2k:ip --manifest-in tests/golden/manifest.json
+(then copy the new files from --out into tests/golden/)
 """
 
 from __future__ import annotations
@@ -189,7 +190,7 @@ def search_goldens(entry: str, manifest: dict, out_dir: str, device: str) -> Non
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--out", default=os.path.join(ROOT, "gpurun_out", "golden"))
+    ap.add_argument("--out", default=os.path.join(ROOT, "golden_out"))
     ap.add_argument("--sets", default=",".join(SEARCH_SETS))
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--no-unit", action="store_true", help="skip the device-function goldens")
