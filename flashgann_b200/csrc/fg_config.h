@@ -4,7 +4,8 @@
 // The knobs that define WHAT the search computes keep the reference's meaning:
 // BLOCK_SIZE is the reference's CTA width and only fixes its derived semantic
 // values (THETA_MAX, SEARCH_WIDTH and the merge-path segment count); the
-// threads this build actually launches per query are FG_WARPS_PER_QUERY.
+// threads this build launches per query are the planner's choice (one warp
+// per query, or a CTA of warps per query for small batches and dims > 256).
 // INTERNAL_TOPK is accepted and reported; as in the reference it does not
 // change results (the beam buffer is sized from the beam argument).
 #pragma once
@@ -66,10 +67,6 @@
 #ifndef FG_HASH_BASE_BITLEN
 #define FG_HASH_BASE_BITLEN 10
 #endif
-// Threads this build launches per query (4 warps = 128 threads).
-#ifndef FG_WARPS_PER_QUERY
-#define FG_WARPS_PER_QUERY 4
-#endif
 
 #define FG_QG_BQUERY 6           // include/common.hpp:17
 #define FG_MAX_BEAM 1024
@@ -89,4 +86,3 @@ static_assert(PHASE1_THETA >= THETA_MIN && PHASE1_THETA <= THETA_MAX, "PHASE1_TH
 static_assert(PHASE2_THETA >= THETA_MIN && PHASE2_THETA <= THETA_MAX, "PHASE2_THETA out of bounds");
 static_assert(PHASE1_RHO >= RHO_MIN && PHASE1_RHO <= RHO_MAX, "PHASE1_RHO out of bounds");
 static_assert(MIN_PHASE2_KEEP > 0, "MIN_PHASE2_KEEP must be > 0");
-static_assert(FG_WARPS_PER_QUERY >= 1 && FG_WARPS_PER_QUERY <= 8, "FG_WARPS_PER_QUERY must be in [1, 8]");
