@@ -116,9 +116,14 @@ __host__ __device__ inline size_t slice_layout(uint32_t padded, uint32_t slots, 
 // bucket), two-choice: a key lives in the emptier of its two buckets, so a
 // lookup reads both (independent loads) and a missing key is settled as soon
 // as either has an empty slot.  Only when both are full does an insert walk on
-// linearly from the second bucket, and a lookup with both full walks the same
-// way (nothing is ever removed between resets, so the walk meets the key
-// before any empty slot).  Two choices keep the walks rare at loads up to ~93 %.
+// linearly from the second bucket; it first sets the overflow flag of that
+// bucket (the MSB of its slot 0: node ids are < 2^31 - 1, so a flagged id
+// never reads as the empty value).  A lookup with both buckets full walks the
+// same way only if the flag is set -- nothing is removed between resets, so
+// the walk meets the key before any empty slot, and with the flag clear no key
+// of that bucket was placed elsewhere.  Two choices keep the walks rare at
+// loads up to ~93 %; the flag spares the lookups of absent keys (most of the
+// walks) that would otherwise have to reach an empty slot.
 __device__ __forceinline__ void w_buckets(uint32_t key, uint32_t nb, uint32_t& b1, uint32_t& b2) {
     b1 = __umulhi(key * 0x9E3779B1u, nb);
     b2 = __umulhi((key ^ 0x5bd1e995u) * 0x85EBCA77u, nb);
@@ -126,7 +131,7 @@ __device__ __forceinline__ void w_buckets(uint32_t key, uint32_t nb, uint32_t& b
 }
 
 __device__ __forceinline__ bool has_key(const uint4& v, uint32_t key) {
-    return v.x == key || v.y == key || v.z == key || v.w == key;
+    return (v.x & ~kMsb) == key || v.y == key || v.z == key || v.w == key;
 }
 
 __device__ __forceinline__ int empties(const uint4& v) {
@@ -149,7 +154,7 @@ __device__ __noinline__ bool w_walk_insert(uint32_t* t, uint32_t nb, uint32_t ke
         b = b + 1 == nb ? 0 : b + 1;
         for (int j = 0; j < 4; ++j) {
             const uint32_t cur = t[4 * b + j];
-            if (cur == key) return false;
+            if ((j == 0 ? (cur & ~kMsb) : cur) == key) return false;
             if (cur == kMax) {
                 const uint32_t old = atomicCAS(&t[4 * b + j], kMax, key);
                 if (old == kMax) return true;
@@ -170,7 +175,10 @@ __device__ __forceinline__ bool w_insert(uint32_t* t, uint32_t slots, uint32_t k
         const uint4 v2 = *reinterpret_cast<const uint4*>(t + 4 * b2);
         if (has_key(v1, key) || has_key(v2, key)) return false;
         const int e1 = empties(v1), e2 = empties(v2);
-        if (e1 == 0 && e2 == 0) return w_walk_insert(t, nb, key, b2);
+        if (e1 == 0 && e2 == 0) {
+            atomicOr(&t[4 * b2], kMsb);  // overflow flag: slot 0 of a full bucket holds an id
+            return w_walk_insert(t, nb, key, b2);
+        }
         const uint32_t b = e1 >= e2 ? b1 : b2;
         const uint4 v = e1 >= e2 ? v1 : v2;
         const int j = v.x == kMax ? 0 : v.y == kMax ? 1 : v.z == kMax ? 2 : 3;
@@ -189,13 +197,66 @@ __device__ __forceinline__ bool w_contains(const uint32_t* t, uint32_t slots, ui
     const uint4 v1 = *reinterpret_cast<const uint4*>(t + 4 * b1);
     const uint4 v2 = *reinterpret_cast<const uint4*>(t + 4 * b2);
     if (has_key(v1, key) || has_key(v2, key)) return true;
-    if (empties(v1) || empties(v2)) return false;
+    if (empties(v1) || empties(v2) || !(v2.x & kMsb)) return false;
     return w_walk_contains(t, nb, key, b2);
 }
 
 __device__ __forceinline__ void w_clear(uint32_t* t, uint32_t slots, int lane) {
     const uint4 e = make_uint4(kMax, kMax, kMax, kMax);
     for (uint32_t i = static_cast<uint32_t>(lane) * 4; i < slots; i += 128) *reinterpret_cast<uint4*>(t + i) = e;
+}
+
+// ----------------------------------------------------------- parent blocks
+// Read-only loads as volatile inline PTX: they stay where they are written, so
+// the next parent's block is in flight while the current one is examined (a
+// plain read-only load may legally be sunk to its first use).
+__device__ __forceinline__ uint32_t ldg_pinned(const void* p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint4 ldg_pinned_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// load_parent (fg_device.cuh) with pinned loads: neighbour id, the three
+// factors and the packed code words of neighbour `lane` of the parent row.
+template <int W>
+__device__ __forceinline__ void load_parent_pinned(const float* __restrict__ prow, const SearchArgs& a, int limit,
+                                                   bool vec, int lane, ParentLane<W>& p) {
+    const uint32_t* ids = reinterpret_cast<const uint32_t*>(prow + a.nbr_off);
+    const float* fac = prow + a.factor_off;
+    p.child = kMax;
+    p.tx = FLT_MAX;
+    p.fdq = 0.0f;
+    p.fvq = 0.0f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) p.c[w] = 0;
+    if (lane < limit) {
+        p.child = ldg_pinned(ids + lane);
+        p.tx = __uint_as_float(ldg_pinned(fac + lane));
+        p.fdq = __uint_as_float(ldg_pinned(fac + a.degree + lane));
+        p.fvq = __uint_as_float(ldg_pinned(fac + 2 * a.degree + lane));
+        const uint32_t* code = reinterpret_cast<const uint32_t*>(prow + a.code_off) + static_cast<size_t>(lane) * W;
+        if constexpr (W % 4 == 0) {
+            if (vec) {
+#pragma unroll
+                for (int w = 0; w < W; w += 4) {
+                    const uint4 x = ldg_pinned_v4(code + w);
+                    p.c[w] = x.x;
+                    p.c[w + 1] = x.y;
+                    p.c[w + 2] = x.z;
+                    p.c[w + 3] = x.w;
+                }
+                return;
+            }
+        }
+#pragma unroll
+        for (int w = 0; w < W; ++w) p.c[w] = ldg_pinned(code + w);
+    }
 }
 
 // ------------------------------------------------------------ exact distances
@@ -778,7 +839,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
             const float* prow = rows + static_cast<uint64_t>(s.pnode[0]) * rowf;
             const float pd = s.pdist[0];
             ParentLane<W> p;
-            load_parent<W>(prow, a, static_cast<int>(work), vec, lane, p);
+            load_parent_pinned<W>(prow, a, static_cast<int>(work), vec, lane, p);
             const bool in_work = static_cast<uint32_t>(lane) < work;
             uint32_t child = p.child;
             if (child != kMax && (child >= a.n || w_contains(s.hash, slots, child))) child = kMax;
@@ -845,13 +906,13 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
             // one parent per step; the next parent's block is loaded while
             // this one is examined (the last step reloads its own block)
             ParentLane<W> cur;
-            load_parent<W>(rows + static_cast<uint64_t>(s.pnode[0]) * rowf, a, deg, vec, lane, cur);
+            load_parent_pinned<W>(rows + static_cast<uint64_t>(s.pnode[0]) * rowf, a, deg, vec, lane, cur);
             uint32_t total = 0;
 #pragma unroll 1
             for (int t = 0; t < static_cast<int>(num); ++t) {
                 const int tn = t + 1 < static_cast<int>(num) ? t + 1 : t;
                 ParentLane<W> nxt;
-                load_parent<W>(rows + static_cast<uint64_t>(s.pnode[tn]) * rowf, a, deg, vec, lane, nxt);
+                load_parent_pinned<W>(rows + static_cast<uint64_t>(s.pnode[tn]) * rowf, a, deg, vec, lane, nxt);
                 const uint32_t child = cur.child;
                 bool valid = child != kMax && child < a.n && !w_contains(s.hash, slots, child);
                 const uint32_t raw_valid = __popc(__ballot_sync(kFull, valid));
