@@ -833,6 +833,13 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
         const float rho = c.rho;
         const bool cut_ok = isfinite(cutoff) && cutoff < FLT_MAX;
 
+        // both expansion paths end in one exact-distance call: the rows of
+        // ev_nodes[0..ev_n) into s.cdist[ev_slot ? ev_slot[e] : e] (one copy
+        // of the distance rounds keeps the loop's code small; warps of an SM
+        // run both paths at the same time)
+        const uint32_t* ev_nodes;
+        const uint32_t* ev_slot;
+        int ev_n;
         if (!(th > 1)) {
             // ---------------------------- single expander (src/adaptive_search.cuh:221-343)
             const uint32_t work = static_cast<uint32_t>(deg) < cbs ? static_cast<uint32_t>(deg) : cbs;
@@ -893,8 +900,9 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
             __syncwarp();
             const int ne = __popc(ib);
             c_eval += ne;
-            eval_nodes<W, G, IP>(rows, rowf, dim, qr, s.stage, ne, s.cdist, s.eslot, lane);
-            __syncwarp();
+            ev_nodes = s.stage;
+            ev_slot = s.eslot;
+            ev_n = ne;
         } else {
             // ----------------------- speculative expanders (src/adaptive_search.cuh:344-444)
             // degree <= 32: lane l holds neighbour l of every parent; every
@@ -964,9 +972,12 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
             if (ins && slot < pl.collect_cap) s.cidx[slot] = child;
             __syncwarp();
             c_eval += ne;
-            eval_nodes<W, G, IP>(rows, rowf, dim, qr, s.cidx, static_cast<int>(ne), s.cdist, nullptr, lane);
-            __syncwarp();
+            ev_nodes = s.cidx;
+            ev_slot = nullptr;
+            ev_n = static_cast<int>(ne);
         }
+        eval_nodes<W, G, IP>(rows, rowf, dim, qr, ev_nodes, ev_n, s.cdist, ev_slot, lane);
+        __syncwarp();
     }
     // final merge (src/adaptive_search.cuh:448-452)
     if constexpr (mp) {
