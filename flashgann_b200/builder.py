@@ -136,6 +136,12 @@ SPECS = {
                            (100, 256), seed=15),
     "t_1k1536": DatasetSpec("t_1k1536", 1_000, 24, 1536, 1, 0.0, 0.0, 0.0, 32, 10,
                             (32, 128), seed=16, kind="lowrank"),
+    # ragged dimensions for the one-warp-per-query kernel: 50 -> 64 (two code words per
+    # neighbour) and 130 -> 256 (rows and codes not 16-byte aligned: scalar code loads)
+    "t_2k50": DatasetSpec("t_2k50", 2_000, 48, 50, 4, 25.0, 0.0, 255.0, 32, 100,
+                          (64, 128, 256), seed=18),
+    "t_2k130": DatasetSpec("t_2k130", 2_000, 48, 130, 4, 25.0, 0.0, 255.0, 32, 100,
+                           (64, 128, 256), seed=19),
 }
 
 

@@ -20,6 +20,9 @@ CASES = [
     # padded dimension 512 and 2048: the one-CTA-per-query kernel
     ("t_2k300", (100, 256)),
     ("t_1k1536", (32, 128)),
+    # ragged dimensions: padded 64 (W = 2) and 130 -> 256 with unaligned code rows (scalar loads)
+    ("t_2k50", (64, 128, 256)),
+    ("t_2k130", (64, 128, 256)),
 ]
 
 
