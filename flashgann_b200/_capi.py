@@ -65,6 +65,7 @@ SIGNATURES = [
     ("fg_query_prepare_device", ctypes.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     ("fg_beam_merge_device", ctypes.c_int, [_vp, _vp, _i32, _i32, _i32, _i32, _vp]),
     ("fg_effective_sort_beam_size", _u32, [_u32]),
+    ("fg_entry_point_centroid", _u32, [_vp, _u64, _u64, _u64, _i32]),
     ("fg_compute_recall", ctypes.c_float, [_vp, _vp, _u64, _i32, _i32]),
     ("fg_append_run_stats_csv", ctypes.c_int, [_cs, _i32, _i32, _f64, _f64, _f64, _f64]),
     ("fg_infer_metric_from_path", _i32, [_cs]),

@@ -642,6 +642,11 @@ int fg_beam_merge_device(uint32_t* d_idx, float* d_dist, int32_t ncase, int32_t 
 
 uint32_t fg_effective_sort_beam_size(uint32_t beam) { return fg::effective_sort_beam(beam); }
 
+uint32_t fg_entry_point_centroid(const float* rows, uint64_t n, uint64_t dim, uint64_t row, int32_t metric) {
+    if (!rows || n == 0 || dim == 0 || row < dim) return 0xFFFFFFFFu;
+    return centroid_entry(rows, n, dim, row, metric);
+}
+
 float fg_compute_recall(const uint32_t* pred, const int32_t* gt, uint64_t nq, int32_t topk, int32_t gt_k) {
     uint64_t correct = 0;
     const int ek = std::min(topk, gt_k);

@@ -166,6 +166,15 @@ int fg_beam_merge_device(uint32_t* d_idx, float* d_dist, int32_t ncase, int32_t 
 /* include/utils.cuh:119-127 */
 uint32_t fg_effective_sort_beam_size(uint32_t beam);
 
+/* include/common.hpp:26-47: the entry point a codebook gets when its header
+ * holds UINT32_MAX -- the node whose raw vector (the first dim floats of each
+ * row of row_floats floats) is nearest the centroid of all raw vectors (largest
+ * inner product for FG_METRIC_IP), the first such node on ties.  fg_index_load
+ * and fg_index_create apply it.  Returns UINT32_MAX for invalid arguments
+ * (NULL rows, num_nodes or dim 0, row_floats < dim). */
+uint32_t fg_entry_point_centroid(const float* rows, uint64_t num_nodes, uint64_t dim, uint64_t row_floats,
+                                 int32_t metric);
+
 /* include/common.hpp:49-66: recall of predicted[nq*topk] against
  * groundtruth[nq*gt_k]; duplicates in a prediction row are all counted. */
 float fg_compute_recall(const uint32_t* predicted, const int32_t* groundtruth, uint64_t nq, int32_t topk,

@@ -12,7 +12,7 @@ import struct
 import numpy as np
 import pytest
 
-from tests.common import ROOT
+from tests.common import ROOT, dataset
 
 
 def _declared_symbols():
@@ -157,3 +157,48 @@ def test_cli_argument_errors():
     assert r.returncode == 1 and "Unknown argument: -bogus" in r.stderr
     r = subprocess.run([exe, "/missing/a", "b", "c", "d"], capture_output=True, text=True)
     assert r.returncode == 1 and "cannot open" in r.stderr
+
+
+def test_entry_point_centroid_matches_oracle():
+    """fg_entry_point_centroid (the UINT32_MAX entry-point fallback of
+    include/common.hpp:26-47) equals the oracle's restatement on seeded data,
+    reads only the first dim floats of each row, and keeps the first node on ties."""
+    import ctypes
+    import numpy as np
+    import flashgann_b200 as fg
+    import oracle
+    L = fg.lib()
+    O = oracle.lib()
+    f32p = ctypes.POINTER(ctypes.c_float)
+
+    def both(rows, dim, metric):
+        rows = np.ascontiguousarray(rows, dtype=np.float32)
+        n, row = rows.shape
+        got = L.fg_entry_point_centroid(rows.ctypes.data_as(ctypes.c_void_p), n, dim, row, metric)
+        want = O.og_entry_point_centroid(rows.ctypes.data_as(f32p), n, dim, row, metric)
+        return int(got), int(want)
+
+    rng = np.random.default_rng(7)
+    ds = dataset("t_2k")
+    for metric in (fg.FG_METRIC_L2, fg.FG_METRIC_IP):
+        got, want = both(ds.rows, ds.spec.dim, metric)
+        assert got == want
+    # float data, rows wider than dim with noise after the raw vector
+    x = rng.standard_normal((3000, 40)).astype(np.float32)
+    x[:, 33:] = rng.uniform(-1e6, 1e6, (3000, 7))
+    for metric in (fg.FG_METRIC_L2, fg.FG_METRIC_IP):
+        got, want = both(x, 33, metric)
+        assert got == want
+    # the L2 choice is the float64 argmin on well separated data
+    y = rng.integers(0, 256, (500, 64)).astype(np.float32)
+    c = y.astype(np.float64).mean(0)
+    d = ((y - c) ** 2).sum(1)
+    if np.partition(d, 1)[1] - d.min() > 1.0:
+        assert both(y, 64, fg.FG_METRIC_L2)[0] == int(np.argmin(d))
+    # identical rows: the first node
+    assert both(np.ones((50, 36), dtype=np.float32), 36, fg.FG_METRIC_L2) == (0, 0)
+    # invalid arguments
+    assert L.fg_entry_point_centroid(None, 10, 8, 8, 0) == 0xFFFFFFFF
+    z = np.zeros((4, 8), dtype=np.float32)
+    assert L.fg_entry_point_centroid(z.ctypes.data_as(ctypes.c_void_p), 4, 8, 7, 0) == 0xFFFFFFFF
+    assert L.fg_entry_point_centroid(z.ctypes.data_as(ctypes.c_void_p), 0, 8, 8, 0) == 0xFFFFFFFF
