@@ -14,7 +14,7 @@ CSRC    := flashgann_b200/csrc
 LIB     := flashgann_b200/libflashgann.so
 BIN_DIR := bin
 
-KERNEL_SRC := $(CSRC)/fg_search.cu $(CSRC)/fg_search_warp.cu $(CSRC)/fg_api.cu
+KERNEL_SRC := $(CSRC)/fg_search.cu $(CSRC)/fg_search_warp.cu $(CSRC)/fg_shard_merge.cu $(CSRC)/fg_api.cu
 HEADERS    := $(CSRC)/fg_config.h $(CSRC)/fg_internal.h $(CSRC)/fg_device.cuh include/flashgann.h
 OBJ_DIR    := flashgann_b200/_build
 OBJS       := $(patsubst $(CSRC)/%.cu,$(OBJ_DIR)/%.o,$(KERNEL_SRC))
@@ -40,8 +40,11 @@ $(BIN_DIR):
 
 gpu_flashgann: $(BIN_DIR)/gpu_flashgann
 
+# nvcc drives the host compiler for the CLI too, as the reference's Makefile
+# does for main.cu, so every EXTRA_NVFLAGS a reference build accepts
+# (-DINTERNAL_TOPK=..., -Xptxas ..., -Xcompiler ...) is valid here as well
 $(BIN_DIR)/gpu_flashgann: $(CSRC)/fg_cli.cpp $(LIB) | $(BIN_DIR)
-	$(CXX) -std=c++17 -O2 $(EXTRA_NVFLAGS) -o $@ $(CSRC)/fg_cli.cpp -L$(dir $(LIB)) -lflashgann -Wl,-rpath,'$$ORIGIN/../flashgann_b200'
+	$(NVCC) $(NVFLAGS) -o $@ $(CSRC)/fg_cli.cpp -L$(dir $(LIB)) -lflashgann -Xlinker -rpath,'$$ORIGIN/../flashgann_b200'
 
 oracle:
 	$(MAKE) -C oracle

@@ -2,12 +2,15 @@
 degree-32 seeded synthetic config.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl flashgann|reference]
+                    [--config NAME] [--scaling weak|strong] [--mode replicated|sharded]
 
-One step = one search of the config's 10,000-query batch at the smallest beam
-of the config's beam list whose recall@100 reaches 0.95 (calibrated before
-timing, untimed).  Each rank searches its own full batch on its own GPU with
-the index replicated (queries partition, no collective on the data path:
-weak scaling); rank 0 prints one JSON line.
+One step = one search of a query batch at the smallest beam of the config's
+beam list whose recall reaches 0.95 (the whole recall-vs-beam curve is
+measured first, untimed, and printed).  The index is replicated on every GPU
+and the queries are partitioned, with no collective on the data path:
+--scaling weak (default) gives every rank a distinct batch of the config's
+size (rank 0's is the config's own batch); --scaling strong splits the
+config's one batch into N slices.  Rank 0 prints one JSON line.
 
 --impl reference runs the reference's algorithm on the host cores (the C
 oracle port with OpenMP; the reference itself has no CPU path) on a bounded
@@ -178,17 +181,15 @@ def _interpolate(table, beam, qps_at):
     return {"recall": TARGET_RECALL, "qps": q0 + w * (q1 - q0), "beams": [b0, beam], "qps_at_beams": [q0, q1]}
 
 
-def _calibrate(run, gt, K, beams):
-    """Smallest beam of the config list reaching the target recall."""
-    import flashgann_b200 as fg
-    table = []
-    for beam in beams:
-        ids = run(beam)
-        r = fg.compute_recall(ids, gt, K)
-        table.append((beam, r))
-        if r >= TARGET_RECALL:
-            return beam, r, table
-    return beams[-1], table[-1][1], table
+def _calibrate(run, gt, K, beams, recall_fn):
+    """The recall-vs-beam curve over every beam of the config's list, and the
+    smallest beam whose recall reaches the target (the last beam if none
+    does).  Every beam runs, so every rank makes the same calls (recall_fn
+    may be a collective)."""
+    table = [(beam, recall_fn(run(beam), gt, K)) for beam in beams]
+    hit = [b for b, r in table if r >= TARGET_RECALL]
+    beam = hit[0] if hit else beams[-1]
+    return beam, dict(table)[beam], table
 
 
 def cpu_baseline(ds, beam, budget_s=12.0, threads=0):
@@ -208,7 +209,35 @@ def cpu_baseline(ds, beam, budget_s=12.0, threads=0):
             "sample": f"first {n} of {len(ds.queries)} queries at beam {beam}, {dt:.1f} s on {cores} threads"}, ids
 
 
+def _workload_config(spec, total_q, beam, ws, scaling):
+    """The `config` object of both arms: the workload only (results go elsewhere)."""
+    from flashgann_b200 import builder
+    L = builder.layout(spec.dim, spec.degree)
+    if scaling == "strong":
+        par = f"queries partitioned: one {total_q}-query batch split over {ws} GPU(s), index replicated"
+    else:
+        par = f"queries partitioned: a distinct {total_q // ws}-query batch per GPU, index replicated x{ws}"
+    return {"workload": spec.name, "n": spec.n, "dim": spec.dim, "degree": spec.degree, "K": spec.K,
+            "queries_total": total_q, "beam": beam, "parallelism": par,
+            "l2": "inputs larger than L2 (codebook %.2f GB > 126 MB)" % (spec.n * L.row * 4 / 1e9)}
+
+
+def _sum_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def run_flashgann(args, ws, rank, local):
+    """Replicated index, queries partitioned over the ranks.  weak: every
+    rank searches a batch of its own (query set `rank` of the config, each
+    spec.nq queries; rank 0's is the config's own batch), so per-GPU work is
+    fixed as N grows; strong: the config's one batch is split into N
+    contiguous slices.  Recall is over all ranks' queries."""
     import torch
     import flashgann_b200 as fg
     from flashgann_b200 import builder
@@ -221,12 +250,21 @@ def run_flashgann(args, ws, rank, local):
     if rank != 0:
         ds = builder.materialize(args.config, device=dev)
     spec = ds.spec
-    if args.queries:
-        ds.queries = ds.queries[:args.queries]
-        ds.gt = ds.gt[:args.queries]
-    K, nq = spec.K, len(ds.queries)
+    strong = args.scaling == "strong"
+    if strong:
+        queries, gt = ds.queries, ds.gt
+        if args.queries:
+            queries, gt = queries[:args.queries], gt[:args.queries]
+        lo, hi = builder.shard_range(len(queries), ws, rank)
+        queries, gt = queries[lo:hi], gt[lo:hi]
+    else:
+        queries, gt = builder.query_set(ds, rank, device=dev, verbose=True)
+        if args.queries:
+            queries, gt = queries[:args.queries], gt[:args.queries]
+    K, nq = spec.K, len(queries)
+    total_q = _sum_over_ranks(float(nq), ws)
     qg = fg.QuantizationGraph(spec.n, spec.dim, spec.degree, ds.codebook_path, device=local)
-    dq = torch.from_numpy(ds.queries).to(dev)
+    dq = torch.from_numpy(np.ascontiguousarray(queries)).to(dev)
     dout = torch.empty((nq, K), dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
 
@@ -235,9 +273,15 @@ def run_flashgann(args, ws, rank, local):
         torch.cuda.synchronize()
         return dout.cpu().numpy().view(np.uint32)
 
-    beam, recall, table = (args.beam, None, []) if args.beam else _calibrate(run_dev, ds.gt, K, spec.beams)
-    if recall is None:
-        recall = fg.compute_recall(run_dev(beam), ds.gt, K)
+    def recall_all(ids, g, k):
+        # hits over every rank's queries
+        return _sum_over_ranks(fg.compute_recall(ids, g, k) * len(ids) * k, ws) / (total_q * k)
+
+    if args.beam:
+        beam, table = args.beam, []
+        recall = recall_all(run_dev(beam), gt, K)
+    else:
+        beam, recall, table = _calibrate(run_dev, gt, K, spec.beams, recall_all)
     # counters of one pass (traversal is deterministic) for the roofline
     dstats = torch.zeros((nq, 4), dtype=torch.int32, device=dev)
     qg.search_device(dq, K, beam, d_out=dout, stream=stream, d_stats=dstats)
@@ -268,7 +312,7 @@ def run_flashgann(args, ws, rank, local):
 
     def qps_at(b):
         if b == beam:
-            return ws * nq / (ms_max / 1e3)
+            return total_q / (ms_max / 1e3)
         for _ in range(2):
             qg.search_device(dq, K, b, d_out=dout, stream=stream)
         torch.cuda.synchronize()
@@ -279,12 +323,12 @@ def run_flashgann(args, ws, rank, local):
             qg.search_device(dq, K, b, d_out=dout, stream=stream)
         e1.record(stream)
         torch.cuda.synchronize()
-        return ws * nq / (_max_over_ranks(e0.elapsed_time(e1) / 3, ws) / 1e3)
+        return total_q / (_max_over_ranks(e0.elapsed_time(e1) / 3, ws) / 1e3)
 
     interp = _interpolate(table, beam, qps_at)
 
     # end to end through the public host-buffer API (pinned host memory)
-    hq = torch.from_numpy(ds.queries).pin_memory().numpy()
+    hq = torch.from_numpy(np.ascontiguousarray(queries)).pin_memory().numpy()
     hres = torch.empty((nq, K), dtype=torch.int32).pin_memory().numpy().view(np.uint32)
     for _ in range(max(1, args.warmup // 2)):
         qg.gpu_search_adaptive(nq, hq, K, hres, beam)
@@ -296,7 +340,7 @@ def run_flashgann(args, ws, rank, local):
     e2e_max = _max_over_ranks(e2e_s, ws)
     qg.close()
 
-    value = ws * nq / (ms_max / 1e3)
+    value = total_q / (ms_max / 1e3)
     peak, peak_kind = _peaks()
     achieved = graded_bytes / (ms / 1e3) / 1e9
     traffic = _traffic_per_query()
@@ -305,14 +349,11 @@ def run_flashgann(args, ws, rank, local):
     out = {
         "metric": _metric_name(spec),
         "value": value, "unit": "queries/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms_max, "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "f32", "data": _data_name(spec),
-        "config": {"workload": spec.name, "n": spec.n, "dim": spec.dim, "degree": spec.degree, "K": K,
-                   "queries_per_gpu": nq, "beam": beam, "recall_at_k": recall,
-                   "recall_table": table, "qps_interpolated_to_target_recall": interp,
-                   "parallelism": f"queries partitioned, index replicated x{ws}",
-                   "l2": "inputs larger than L2 (codebook %.2f GB > 126 MB)" % (spec.n * L.row * 4 / 1e9)},
-        "e2e": {"value": ws * nq / e2e_max, "unit": "queries/s",
+        "config": _workload_config(spec, int(total_q), beam, ws, args.scaling),
+        "recall": {"at_beam": recall, "curve": table, "qps_interpolated_to_target_recall": interp},
+        "e2e": {"value": total_q / e2e_max, "unit": "queries/s",
                 "h2d_bytes_per_step": nq * spec.dim * 4, "d2h_bytes_per_step": nq * K * 4},
         "gpu_launches": args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -356,18 +397,23 @@ def run_sharded(args, ws, rank, local):
     dd = torch.empty((nq, K), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream()
 
+    offsets = [builder.shard_range(spec.n, ws, r)[0] for r in range(ws)]
+    assert offsets[rank] == sh.offset
+
     def step(beam, q=dq):
         qg.search_device(q, K, beam, d_out=dout, d_dists=dd, stream=stream)
-        return fgd.gather_shard_topk(dout, dd, K, sh.offset)
+        return fgd.gather_shard_topk(dout, dd, K, offsets)
 
     def run(beam):
         ids, _ = step(beam)
         torch.cuda.synchronize()
-        return ids.cpu().numpy().astype(np.uint32)
+        return ids.cpu().numpy().view(np.uint32)
 
-    beam, recall, table = (args.beam, None, []) if args.beam else _calibrate(run, gt, K, spec.beams)
-    if recall is None:
+    if args.beam:
+        beam, table = args.beam, []
         recall = fg.compute_recall(run(beam), gt, K)
+    else:
+        beam, recall, table = _calibrate(run, gt, K, spec.beams, fg.compute_recall)
     for _ in range(args.warmup):
         step(beam)
     torch.cuda.synchronize()
@@ -386,7 +432,7 @@ def run_sharded(args, ws, rank, local):
     ms_max = _max_over_ranks(ms, ws)
     # end to end: pinned host queries in, merged ids out, every step
     hq = torch.from_numpy(queries).pin_memory()
-    hres = torch.empty((nq, K), dtype=torch.int64).pin_memory()
+    hres = torch.empty((nq, K), dtype=torch.int32).pin_memory()
     _barrier(ws)
     t0 = time.perf_counter()
     for _ in range(args.steps):
@@ -406,15 +452,22 @@ def run_sharded(args, ws, rank, local):
                    "recall_table": table,
                    "parallelism": f"index sharded x{ws} (per-shard graphs), all-gather of per-shard top-{K} + device merge"},
         "e2e": {"value": nq / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": nq * spec.dim * 4,
-                "d2h_bytes_per_step": nq * K * 8},
-        "gpu_launches": args.steps,
+                "d2h_bytes_per_step": nq * K * 4},
+        "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
 
 
 def run_reference(args, ws, rank, local):
+    """The reference arm.  Its value is the reference's algorithm on the host
+    cores (the reference itself has no CPU path, so the C oracle port with
+    OpenMP) on a bounded sample; beside it, key reference_gpu, the
+    reference's own sm_100a build (oracle/_ref, QuantizationGraph::
+    gpu_search_adaptive, index upload excluded as the reference times it) on
+    the same batch, with its recall-vs-beam curve.  Recall is scored by the
+    oracle, so this arm loads no library of this build."""
+    import oracle
     from flashgann_b200 import builder
-    import flashgann_b200 as fg
     if rank != 0:
         return None
     import torch
@@ -430,7 +483,8 @@ def run_reference(args, ws, rank, local):
             g = ref.RefGraph(ds.codebook_path, spec.n, spec.dim, spec.degree)
             ref_table = []
             if not beam:
-                beam, _, ref_table = _calibrate(lambda b: g.search(ds.queries, K, b)[0], ds.gt, K, spec.beams)
+                beam, _, ref_table = _calibrate(lambda b: g.search(ds.queries, K, b)[0], ds.gt, K, spec.beams,
+                                                oracle.compute_recall)
             ids, _ = g.search(ds.queries, K, beam)
             times = []
             for _ in range(max(1, args.steps)):
@@ -450,7 +504,7 @@ def run_reference(args, ws, rank, local):
             extra["reference_gpu"] = {
                 "what": "reference sm_100a build, QuantizationGraph::gpu_search_adaptive, 1 GPU",
                 "value": nq / el, "unit": "queries/s", "beam": beam,
-                "recall_at_k": fg.compute_recall(ids, ds.gt, K) if os.path.exists(fg._capi.LIB_PATH) else None,
+                "recall_at_k": oracle.compute_recall(ids, ds.gt, K), "recall_table": ref_table,
                 "elapsed_s": el, "call_s_including_index_upload": call,
                 "qps_interpolated_to_target_recall": ref_interp}
     except Exception as e:  # the CPU leg below is the contract's reference arm
@@ -467,8 +521,8 @@ def run_reference(args, ws, rank, local):
     out = {
         "impl": "reference", "metric": _metric_name(spec), "value": value,
         "unit": "queries/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": _data_name(spec),
-        "config": {"workload": spec.name, "n": spec.n, "dim": spec.dim, "degree": spec.degree, "K": K, "beam": beam},
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": _data_name(spec),
+        "config": _workload_config(spec, nq, beam, 1, args.scaling),
         "cpu_baseline": cb, "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
                                     "d2h_bytes_per_step": 0},
     }
@@ -489,6 +543,9 @@ def main():
     ap.add_argument("--mode", default="replicated", choices=["replicated", "sharded"],
                     help="replicated: index on every GPU, queries partitioned (default); "
                          "sharded: one index shard per GPU, top-K gathered and merged")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="replicated mode over N GPUs: weak = a distinct batch per GPU (default), "
+                         "strong = the config's one batch split over the GPUs")
     ap.add_argument("--queries", type=int, default=0,
                     help="search only the first N queries of the batch (small cases for profiler captures)")
     args = ap.parse_args()

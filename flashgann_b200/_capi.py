@@ -64,6 +64,7 @@ SIGNATURES = [
     ("fg_search_device_ex", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _i32]),
     ("fg_query_prepare_device", ctypes.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     ("fg_beam_merge_device", ctypes.c_int, [_vp, _vp, _i32, _i32, _i32, _i32, _vp]),
+    ("fg_shard_merge_device", ctypes.c_int, [_vp, _vp, ctypes.POINTER(_u32), _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
     ("fg_effective_sort_beam_size", _u32, [_u32]),
     ("fg_entry_point_centroid", _u32, [_vp, _u64, _u64, _u64, _i32]),
     ("fg_compute_recall", ctypes.c_float, [_vp, _vp, _u64, _i32, _i32]),

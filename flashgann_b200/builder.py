@@ -151,6 +151,19 @@ def _rng(seed: int, stream: int) -> np.random.Generator:
 
 def generate_vectors(spec: DatasetSpec) -> Tuple[np.ndarray, np.ndarray]:
     """Base and query vectors (float32) for a spec; deterministic in the seed."""
+    return _draw(spec, 1, spec.n), _draw(spec, 2, spec.nq)
+
+
+def generate_queries(spec: DatasetSpec, index: int) -> np.ndarray:
+    """Query set `index` of a spec: 0 is the dataset's own batch, index > 0
+    draws spec.nq further queries from the same distribution with a stream
+    of their own (distinct batches for the ranks of a multi-GPU run)."""
+    return _draw(spec, 2 if index == 0 else 1000 + index, spec.nq)
+
+
+def _draw(spec: DatasetSpec, stream: int, m: int) -> np.ndarray:
+    """m vectors of the spec's distribution from RNG stream `stream`
+    (stream 0 holds the distribution's parameters, 1 the base, 2 the queries)."""
     if spec.kind == "int_gmm":
         cr = _rng(spec.seed, 0)
         centres = cr.uniform(spec.lo, spec.hi, size=(spec.n_comp, spec.dim))
@@ -169,7 +182,7 @@ def generate_vectors(spec: DatasetSpec) -> Tuple[np.ndarray, np.ndarray]:
                 out[s:e] = v
             return out
 
-        return draw(1, spec.n), draw(2, spec.nq)
+        return draw(stream, m)
     if spec.kind == "norm_aniso":
         cr = _rng(spec.seed, 0)
         centres = cr.standard_normal((spec.n_comp, spec.dim))
@@ -182,13 +195,14 @@ def generate_vectors(spec: DatasetSpec) -> Tuple[np.ndarray, np.ndarray]:
             v /= np.linalg.norm(v, axis=1, keepdims=True)
             return v.astype(np.float32)
 
-        return draw(1, spec.n), draw(2, spec.nq)
+        return draw(stream, m)
     if spec.kind == "int_gmm_dup":
         # every base vector repeated 4 times (consecutive ids): long runs of
         # equal distances, for the merges' tie paths
         uniq = dataclasses.replace(spec, n=(spec.n + 3) // 4, kind="int_gmm")
-        base, queries = generate_vectors(uniq)
-        return np.repeat(base, 4, axis=0)[:spec.n].copy(), queries
+        if stream != 1:
+            return _draw(uniq, stream, m)
+        return np.repeat(_draw(uniq, 1, uniq.n), 4, axis=0)[:m].copy()
     if spec.kind == "lowrank":
         # rank-64 latent x a fixed 64 x dim map + N(0, 0.02^2), L2-normalised
         cr = _rng(spec.seed, 0)
@@ -207,7 +221,7 @@ def generate_vectors(spec: DatasetSpec) -> Tuple[np.ndarray, np.ndarray]:
                 out[s0:e] = v
             return out
 
-        return draw(1, spec.n), draw(2, spec.nq)
+        return draw(stream, m)
     raise ValueError(f"unknown dataset kind {spec.kind}")
 
 
@@ -587,6 +601,31 @@ def materialize(name_or_spec, cache_dir: Optional[str] = None, device=None,
     if verbose:
         print(f"[builder] {spec.name}: done {time.time() - t0:.1f}s", flush=True)
     return Dataset(spec, base, queries, gt, rows, signs, entry, L, paths["cb"], d)
+
+
+def query_set(ds: Dataset, index: int, device=None, cache_dir: Optional[str] = None,
+              verbose: bool = False) -> Tuple[np.ndarray, np.ndarray]:
+    """Query batch `index` of a materialised dataset with its exact ground
+    truth (int32 [nq, gt_k]): 0 is the dataset's own batch; index > 0 is a
+    further batch of the same distribution (generate_queries), its ground
+    truth computed like the dataset's and cached beside it."""
+    if index == 0:
+        return ds.queries, ds.gt
+    spec = ds.spec
+    d = os.path.join(cache_dir or default_cache_dir(), spec.name)
+    qp, gp = os.path.join(d, f"query_set{index}.fvecs"), os.path.join(d, f"gt_set{index}.ivecs")
+    if os.path.exists(qp) and os.path.exists(gp):
+        return read_vecs(qp), read_vecs(gp, np.int32)
+    queries = generate_queries(spec, index)
+    gt_ids, _ = brute_force_knn(ds.base, queries, min(spec.gt_k, spec.n), device=device)
+    gt = gt_ids.astype(np.int32)
+    write_vecs(gp + ".tmp", gt)
+    write_vecs(qp + ".tmp", queries)
+    os.replace(gp + ".tmp", gp)
+    os.replace(qp + ".tmp", qp)
+    if verbose:
+        print(f"[builder] {spec.name}: query set {index} ({len(queries)} queries)", flush=True)
+    return queries, gt
 
 
 # --------------------------------------------------------------------------

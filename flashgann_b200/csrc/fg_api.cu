@@ -162,11 +162,14 @@ void destroy(fg_index* x) {
     delete x;
 }
 
-int check_device(int device) {
+// Checks the device ordinal; FG_DEVICE_CURRENT becomes the calling thread's
+// current device (the device the reference's search uses).
+int check_device(int* device) {
     int count = 0;
     cudaError_t e = cudaGetDeviceCount(&count);
     if (e != cudaSuccess || count < 1) return fail(FG_ERR_NO_DEVICE, "no CUDA device available (%s)", cudaGetErrorString(e));
-    if (device < 0 || device >= count) return fail(FG_ERR_ARG, "device %d outside [0, %d)", device, count);
+    if (*device == FG_DEVICE_CURRENT && (e = cudaGetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (*device < 0 || *device >= count) return fail(FG_ERR_ARG, "device %d outside [0, %d)", *device, count);
     return FG_OK;
 }
 
@@ -246,11 +249,12 @@ int fg_index_load(const char* path, uint64_t n, uint64_t dim, int32_t degree, in
                     (unsigned long long)size, (unsigned long long)n, (unsigned long long)dim, degree,
                     (unsigned long long)need);
     }
-    if ((rc = check_device(device))) {
+    if ((rc = check_device(&device))) {
         fclose(f);
         destroy(x);
         return rc;
     }
+    x->device = device;
     DeviceGuard g(device);
     if (g.err != cudaSuccess) {
         fclose(f);
@@ -313,7 +317,7 @@ int fg_index_create(const float* rows, const float* signs, uint32_t entry, uint6
     *out = nullptr;
     int rc = check_shape(n, dim, degree, metric);
     if (rc) return rc;
-    if ((rc = check_device(device))) return rc;
+    if ((rc = check_device(&device))) return rc;
     auto* x = new fg_index();
     x->device = device;
     x->metric = metric;
@@ -638,6 +642,23 @@ int fg_beam_merge_device(uint32_t* d_idx, float* d_dist, int32_t ncase, int32_t 
         return fail(FG_ERR_ARG, "itopk %d is not an effective sort beam size", itopk);
     cudaError_t e = fg::launch_beam_merge(d_idx, d_dist, ncase, itopk, cbs, first, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? FG_OK : cuda_fail(e, "merge launch");
+}
+
+int fg_shard_merge_device(const uint32_t* d_ids, const float* d_dists, const uint32_t* shard_offsets, int32_t shards,
+                          int32_t nq, int32_t k, int32_t K, uint32_t* d_out_ids, float* d_out_dists, void* stream) {
+    g_err.clear();
+    if (shards < 1 || shards > fg::shard_merge_max_shards())
+        return fail(FG_ERR_ARG, "shards %d outside [1, %d]", shards, fg::shard_merge_max_shards());
+    if (nq < 0 || k < 1 || K < 1) return fail(FG_ERR_ARG, "bad merge shape nq=%d k=%d K=%d", nq, k, K);
+    if (static_cast<int64_t>(shards) * k < K)
+        return fail(FG_ERR_ARG, "%d lists of %d entries cannot fill the top-%d", shards, k, K);
+    if (static_cast<size_t>(shards) * k * sizeof(float) > 227u * 1024u)
+        return fail(FG_ERR_UNSUPPORTED, "%d lists of %d distances exceed one CTA's shared memory", shards, k);
+    if (nq == 0) return FG_OK;
+    if (!d_ids || !d_dists || !d_out_ids) return fail(FG_ERR_ARG, "null buffer");
+    cudaError_t e = fg::launch_shard_merge(d_ids, d_dists, shard_offsets, shards, nq, k, K, d_out_ids, d_out_dists,
+                                           static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? FG_OK : cuda_fail(e, "shard merge launch");
 }
 
 uint32_t fg_effective_sort_beam_size(uint32_t beam) { return fg::effective_sort_beam(beam); }

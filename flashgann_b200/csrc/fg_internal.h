@@ -68,6 +68,11 @@ cudaError_t launch_query_prepare(const float* queries, int nq, int dim, const fl
 cudaError_t launch_beam_merge(uint32_t* idx, float* dist, int ncase, int itopk, int cbs, int first,
                               cudaStream_t stream);
 
+// Per-query merge of a sharded index's top-k lists (fg_shard_merge.cu).
+int shard_merge_max_shards();
+cudaError_t launch_shard_merge(const uint32_t* ids, const float* dists, const uint32_t* offsets, int shards, int nq,
+                               int k, int K, uint32_t* out_ids, float* out_dists, cudaStream_t stream);
+
 // Host restatements shared with the CLI and the API.
 uint32_t effective_sort_beam(uint32_t beam);
 uint32_t candidate_buffer_size(int degree);

@@ -8,7 +8,8 @@ only, gpu_search_adaptive.cu:30-34).  Two modes are provided:
   slices are gathered -- the only collective is that gather of results;
 * sharded index (the 100M config): every rank holds one shard with its own
   graph, searches *all* queries on it, and the per-shard top-K lists
-  (distance, global id) are all-gathered and merged per query.
+  (distance, local id) are all-gathered and merged per query by a CUDA
+  kernel (fg_shard_merge_device) into global ids.
 
 Both work with any torch.distributed backend (NCCL on GPUs, gloo on CPU for
 the tests); the search itself is injected, so the host logic is testable
@@ -67,53 +68,77 @@ def search_partitioned(search: Callable[[np.ndarray], Tuple[np.ndarray, np.ndarr
     return out_i, out_d
 
 
-def merge_shard_topk(dists: torch.Tensor, ids: torch.Tensor, K: int) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Merge per-shard sorted top-K lists into one top-K per query.
+def merge_shard_topk_device(ids: torch.Tensor, dists: torch.Tensor, offsets, K: int,
+                            out_ids: Optional[torch.Tensor] = None,
+                            out_dists: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Global top-K from per-shard sorted lists, on the GPU (the
+    fg_shard_merge_device kernel of libflashgann.so).
 
-    dists/ids: [S, nq, K] (shard-major, each list ascending, global ids).
-    Ties are ordered by shard, then by position in the shard's list, so the
-    result is deterministic.  Returns (ids [nq, K], dists [nq, K])."""
+    ids [S, nq, k] int32 (local ids as the search returns them, uint32 bits),
+    dists [S, nq, k] f32, both CUDA tensors, shard-major, each list
+    ascending; offsets: the S global ids of each shard's node 0.  The merge is
+    the lists' stable merge by (distance, shard, position).  Returns
+    (ids int32 [nq, K] holding uint32 global ids, dists f32 [nq, K]) on the
+    stream torch currently uses."""
+    import ctypes
+    from . import _capi
     S, nq, k = dists.shape
-    d = dists.permute(1, 0, 2).reshape(nq, S * k)
-    i = ids.permute(1, 0, 2).reshape(nq, S * k)
-    order = torch.argsort(d, dim=1, stable=True)[:, :K]
-    return torch.gather(i, 1, order), torch.gather(d, 1, order)
+    if out_ids is None:
+        out_ids = torch.empty((nq, K), dtype=torch.int32, device=dists.device)
+    if out_dists is None:
+        out_dists = torch.empty((nq, K), dtype=torch.float32, device=dists.device)
+    off = (ctypes.c_uint32 * S)(*[int(o) for o in offsets])
+    L = _capi.lib()
+    rc = L.fg_shard_merge_device(_capi.device_ptr(ids.contiguous()), _capi.device_ptr(dists.contiguous()), off, S,
+                                 nq, k, K, _capi.device_ptr(out_ids), _capi.device_ptr(out_dists),
+                                 ctypes.c_void_p(torch.cuda.current_stream(dists.device).cuda_stream))
+    if rc != _capi.FG_OK:
+        raise _capi.FlashGANNError(rc, f"fg_shard_merge_device: {L.fg_last_error().decode()}")
+    return out_ids, out_dists
 
 
 def search_sharded(search: Callable[[np.ndarray], Tuple[np.ndarray, np.ndarray]], queries: np.ndarray, K: int,
-                   shard_offset: int, group=None) -> Tuple[np.ndarray, np.ndarray]:
+                   shard_offset: int, merge: Callable, group=None) -> Tuple[np.ndarray, np.ndarray]:
     """Sharded index: this rank searches all queries on its shard (local ids
-    + shard_offset = global ids); the per-shard lists are all-gathered and
-    merged.  Every rank returns the merged (ids, dists)."""
+    + shard_offset = global ids); the per-shard lists (local ids) and every
+    rank's shard offset are all-gathered and merged by
+    `merge(ids [S, nq, k], dists [S, nq, k], offsets, K) -> (ids, dists)`
+    (merge_shard_topk_device on GPUs).  Every rank returns the merged
+    (ids uint32, dists f32)."""
     world = dist.get_world_size(group)
     ids, dists = search(queries)
     dev = _device_for(group)
-    gi = torch.from_numpy(ids.astype(np.int64) + int(shard_offset)).to(dev)
+    li = torch.from_numpy(np.ascontiguousarray(ids, dtype=np.uint32).view(np.int32)).to(dev)
     gd = torch.from_numpy(np.ascontiguousarray(dists, dtype=np.float32)).to(dev)
-    all_i = [torch.empty_like(gi) for _ in range(world)]
+    offs = torch.tensor([int(shard_offset)], dtype=torch.int64, device=dev)
+    all_i = [torch.empty_like(li) for _ in range(world)]
     all_d = [torch.empty_like(gd) for _ in range(world)]
-    dist.all_gather(all_i, gi, group=group)
+    all_o = [torch.empty_like(offs) for _ in range(world)]
+    dist.all_gather(all_i, li, group=group)
     dist.all_gather(all_d, gd, group=group)
-    mi, md = merge_shard_topk(torch.stack(all_d), torch.stack(all_i), K)
-    return mi.cpu().numpy().astype(np.uint32), md.cpu().numpy()
+    dist.all_gather(all_o, offs, group=group)
+    mi, md = merge(torch.stack(all_i), torch.stack(all_d), [int(o.item()) for o in all_o], K)
+    return mi.cpu().numpy().view(np.uint32).copy(), md.cpu().numpy()
 
 
-def gather_shard_topk(ids: torch.Tensor, dists: torch.Tensor, K: int, shard_offset: int,
-                      group=None) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Device-side merge for a sharded index: this rank's per-query top-K
-    (local ids [nq, K] int32 / uint32 bits, dists [nq, K] f32, on this rank's
-    device) are offset to global ids, all-gathered (NCCL over NVLink on GPUs)
-    and merged into the global top-K on every rank.  Returns (ids int64,
-    dists f32), both [nq, K] on the input device."""
+def gather_shard_topk(ids: torch.Tensor, dists: torch.Tensor, K: int, offsets, group=None,
+                      merge: Callable = merge_shard_topk_device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Device-side step of a sharded index: this rank's per-query top-k
+    (local ids [nq, k] int32 holding uint32 bits, dists [nq, k] f32, on this
+    rank's GPU) are all-gathered (NCCL over NVLink) and merged by the
+    fg_shard_merge_device kernel (or an injected `merge` of the same
+    signature) into the global top-K on every rank; `offsets` lists every
+    rank's shard offset (global id of its node 0).  Returns (ids int32
+    [nq, K] holding uint32 global ids, dists f32 [nq, K])."""
     world = dist.get_world_size(group)
-    gi = (ids.to(torch.int64) & 0xFFFFFFFF) + int(shard_offset)
+    li = ids.contiguous()
     gd = dists.contiguous()
-    nq, k = gi.shape
-    all_i = torch.empty((world * nq, k), dtype=gi.dtype, device=gi.device)
+    nq, k = li.shape
+    all_i = torch.empty((world * nq, k), dtype=li.dtype, device=li.device)
     all_d = torch.empty((world * nq, k), dtype=gd.dtype, device=gd.device)
-    dist.all_gather_into_tensor(all_i, gi, group=group)
+    dist.all_gather_into_tensor(all_i, li, group=group)
     dist.all_gather_into_tensor(all_d, gd, group=group)
-    return merge_shard_topk(all_d.view(world, nq, k), all_i.view(world, nq, k), K)
+    return merge(all_i.view(world, nq, k), all_d.view(world, nq, k), offsets, K)
 
 
 def max_over_ranks(x: float, group=None) -> float:

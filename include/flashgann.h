@@ -34,6 +34,11 @@ extern "C" {
 #define FG_METRIC_L2 0
 #define FG_METRIC_IP 1
 
+/* ---- device argument of fg_index_load / fg_index_create: the calling
+ * thread's current CUDA device, which is where the reference's search runs
+ * (gpu_search_adaptive.cu:30-34) ---- */
+#define FG_DEVICE_CURRENT (-1)
+
 typedef struct fg_index fg_index;
 
 /* Codebook layout in float words, as QuantizationGraph's getters report it
@@ -69,7 +74,8 @@ const char* fg_last_error(void);
  * QuantizationGraph::gpu_search_adaptive (gpu_search_adaptive.cu:46-77):
  * reads the qg_codebook file, resolves entry point UINT32_MAX to the node
  * nearest the centroid (include/common.hpp:26-47), checks free memory and
- * keeps the codebook resident on `device` until fg_index_free. */
+ * keeps the codebook resident on `device` (FG_DEVICE_CURRENT: the current
+ * device) until fg_index_free. */
 int fg_index_load(const char* path, uint64_t num_nodes, uint64_t dim, int32_t degree, int32_t metric,
                   int32_t device, fg_index** out);
 
@@ -125,6 +131,8 @@ int fg_search_multi(fg_index* const* indexes, int32_t count, int32_t nq, const f
  * Limit: 256 + round_up(nq*dim*4, 256) + nq*K*4 <= FG_NOALLOC_SCRATCH_BYTES
  * (e.g. 14,000 queries of dim 128 with K = 10); a larger batch returns
  * FG_ERR_ARG with a message -- split it or call fg_search.
+ * Like fg_search the call is synchronous: it waits for the query upload, the
+ * search and the download of the ids before it returns.
  * The first call on each device looks up the scratch's address on that
  * device; make that first call before any stream capture.  All calls on a
  * device share the one scratch array: calls that overlap in time (from
@@ -160,6 +168,19 @@ int fg_query_prepare_device(const float* d_queries, int32_t nq, int32_t dim, con
  * d_idx/d_dist, merged in place with the reference's tie order. */
 int fg_beam_merge_device(uint32_t* d_idx, float* d_dist, int32_t ncase, int32_t itopk, int32_t cbs, int32_t first,
                          void* stream);
+
+/* Global top-K of a sharded index (the base split into
+ * `shards` parts, each with its own graph): d_ids / d_dists hold, shard-major,
+ * every shard's ascending top-k of the same nq queries ([shards][nq][k],
+ * local ids as fg_search_device returns them, e.g. after an all-gather);
+ * shard_offsets (host, `shards` entries, NULL = all 0) is the global id of
+ * each shard's node 0.  Writes d_out_ids[nq*K] (global ids) and optionally
+ * d_out_dists[nq*K]: the lists' stable merge by (distance, shard, position).
+ * Asynchronous on `stream`.  Needs shards*k >= K and shards <= 64.  No
+ * counterpart in the reference, whose index is one graph on one device
+ * (gpu_search_adaptive.cu:65-72). */
+int fg_shard_merge_device(const uint32_t* d_ids, const float* d_dists, const uint32_t* shard_offsets, int32_t shards,
+                          int32_t nq, int32_t k, int32_t K, uint32_t* d_out_ids, float* d_out_dists, void* stream);
 
 /* ---- host helpers of the reference CLI ---- */
 

@@ -1,5 +1,8 @@
-"""Multi-GPU host logic on CPU: world-size-2 gloo process groups run the
-partitioned and the sharded search with an injected brute-force search."""
+"""Multi-GPU host logic on CPU: world-size-2 and -3 gloo process groups run
+the partitioned and the sharded search with an injected brute-force search
+and, for the sharded index, the plain-torch restatement of the per-query
+merge that fg_shard_merge_device computes on the GPU (the kernel itself is
+checked against it in tests/test_gpu_shard_merge.py)."""
 
 from __future__ import annotations
 
@@ -10,7 +13,8 @@ import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
-from flashgann_b200.distributed import merge_shard_topk, partition
+from flashgann_b200.distributed import partition
+from tests.common import merge_shard_topk_ref
 
 
 def _free_port() -> int:
@@ -41,7 +45,7 @@ def _worker(rank, world, port, mode, out_path):
         ids, d = fgd.search_partitioned(_brute(base, K), queries, K)
     else:
         s, e = fgd.partition(base.shape[0], world, rank)
-        ids, d = fgd.search_sharded(_brute(base[s:e], K), queries, K, shard_offset=s)
+        ids, d = fgd.search_sharded(_brute(base[s:e], K), queries, K, shard_offset=s, merge=merge_shard_topk_ref)
     t = fgd.max_over_ranks(float(rank + 1))
     if rank == 0:
         np.savez(out_path, ids=ids, d=d, t=t)
@@ -77,9 +81,11 @@ def _gather_worker(rank, world, port, out_path):
     queries = np.rint(rng.uniform(0, 255, size=(21, 8))).astype(np.float32)
     s, e = fgd.partition(base.shape[0], world, rank)
     ids, d = _brute(base[s:e], 7)(queries)
-    gi, gd = fgd.gather_shard_topk(torch.from_numpy(ids.view(np.int32)), torch.from_numpy(d), 7, s)
+    offsets = [fgd.partition(base.shape[0], world, r)[0] for r in range(world)]
+    gi, gd = fgd.gather_shard_topk(torch.from_numpy(ids.view(np.int32)), torch.from_numpy(d), 7, offsets,
+                                   merge=merge_shard_topk_ref)
     if rank == 0:
-        np.savez(out_path, ids=gi.numpy(), d=gd.numpy())
+        np.savez(out_path, ids=gi.numpy().view(np.uint32), d=gd.numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -107,9 +113,9 @@ def test_partition_covers_everything():
             assert max(sizes) - min(sizes) <= 1
 
 
-def test_merge_shard_topk_ties_by_shard_then_position():
+def test_merge_reference_ties_by_shard_then_position():
     import torch
     d = torch.tensor([[[1.0, 2.0, 5.0]], [[1.0, 3.0, 4.0]]])
-    i = torch.tensor([[[10, 11, 12]], [[20, 21, 22]]])
-    mi, md = merge_shard_topk(d, i, 4)
+    i = torch.tensor([[[0, 1, 2]], [[0, 1, 2]]], dtype=torch.int32)
+    mi, md = merge_shard_topk_ref(i, d, [10, 20], 4)
     assert mi.tolist() == [[10, 20, 11, 21]] and md.tolist() == [[1.0, 1.0, 2.0, 3.0]]

@@ -73,3 +73,24 @@ def test_cli_recall_and_csv(name, tmp_path):
         runtime, latency, qps = (float(x) for x in row[2:5])
         assert runtime > 0 and qps > 0
         assert np.isclose(latency, runtime * 1e3 / len(ds.queries), rtol=1e-4)
+
+
+COMPAT_EXE = os.path.join(ROOT, "oracle", "_ref", "gpu_flashgann_compat")
+
+
+@pytest.mark.parametrize("name", ["t_2k", "t_8k16"])
+def test_reference_main_against_the_class_drop_in(name):
+    """The reference's own main.cu, compiled unmodified against
+    include/qg_compat.hpp and linked to libflashgann.so (oracle/Makefile,
+    target _ref/gpu_flashgann_compat): its result lines parse, and its recall
+    equals this build's CLI's and is within one hit of the reference CLI's."""
+    if not os.path.exists(COMPAT_EXE):
+        pytest.skip("the class drop-in check is built only where the reference sources are mounted")
+    ds = dataset(name)
+    K = ds.spec.K
+    for beam in (64, 128):
+        got = _run(COMPAT_EXE, ds, K, beam)
+        assert got == _run(EXE, ds, K, beam), f"beam {beam}: class drop-in and CLI recall differ"
+        if os.path.exists(REF_EXE):
+            ref = _run(REF_EXE, ds, K, beam)
+            assert abs(got - ref) <= 100.0 / (len(ds.queries) * K) + 1e-3, f"beam {beam}: {got} vs reference {ref}"

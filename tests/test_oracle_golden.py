@@ -12,7 +12,7 @@ import ctypes
 import numpy as np
 import pytest
 
-from tests.common import dataset, golden, golden_manifest
+from tests.common import compare_with_reference, dataset, golden, golden_manifest
 
 UNIT = golden("ref_unit.npz")
 needs_unit = pytest.mark.skipif(UNIT is None, reason="tests/golden/ref_unit.npz not generated yet")
@@ -105,30 +105,8 @@ def test_controller_rho_and_keep():
         assert ko.value == int(UNIT["ct_keep_out"][i]), i
 
 
-SEARCH_SETS = ["t_2k", "t_8k16", "t_20k", "t_2k_ip"]
-
-
-def tie_order_only(ids, want, base, query, ip=False):
-    """True when two result rows hold the same ids and every position where
-    they differ lies inside a run of equal exact distances (squared L2, or
-    the negated dot product for the inner-product metric)."""
-    if set(ids.tolist()) != set(want.tolist()):
-        return False
-
-    def dist(rows):
-        x = base[rows.astype(np.int64)].astype(np.float64)
-        return -(x @ query) if ip else ((x - query) ** 2).sum(1)
-
-    return np.array_equal(dist(ids), dist(want))
-
-
-def compare_with_reference(ds, ids, want, ip=False):
-    """Queries whose ids differ from the reference beyond tie order, and the
-    number that differ only in the order of equal-distance results."""
-    rows = np.nonzero((ids != want).any(axis=1))[0]
-    ties = [int(i) for i in rows
-            if tie_order_only(ids[i], want[i], ds.base, ds.queries[i].astype(np.float64), ip)]
-    return [int(i) for i in rows if i not in ties], len(ties)
+# c1_100k is BASELINE.json configs[0] at full size (100K nodes, all 1000 queries x 6 beams)
+SEARCH_SETS = ["t_2k", "t_8k16", "t_20k", "t_2k_ip", "c1_100k"]
 
 
 @pytest.mark.parametrize("name", SEARCH_SETS)

@@ -78,3 +78,29 @@ def test_noalloc_rejects_a_batch_beyond_the_scratch():
         assert np.array_equal(_call("fg_search_noalloc", h, small, K, 128), _call("fg_search", h, small, K, 128))
     finally:
         lib().fg_index_free(h)
+
+
+def test_noalloc_on_a_fresh_index_leaves_device_memory_unchanged():
+    """On an index that fg_search has never used (so it owns no query or
+    result buffers), repeated fg_search_noalloc calls leave the device's free
+    memory exactly as it was, and their results still match fg_search's.  The
+    130-d set has rows that are not 16-byte aligned and a query length that
+    is not a multiple of 4 floats, so the staged result ids start right after
+    an odd-sized query block."""
+    import torch
+    from flashgann_b200._capi import lib
+    ds, h = _index("t_2k130")
+    try:
+        K = ds.spec.K
+        q = ds.queries[:33]
+        first = _call("fg_search_noalloc", h, q, K, 128)  # looks up the scratch's address on this device
+        torch.cuda.synchronize()
+        free0, _ = torch.cuda.mem_get_info()
+        outs = [_call("fg_search_noalloc", h, q, K, 128) for _ in range(3)]
+        free1, _ = torch.cuda.mem_get_info()
+        assert free1 == free0, f"free device memory changed by {free0 - free1} bytes"
+        for o in outs:
+            assert np.array_equal(o, first)
+        assert np.array_equal(first, _call("fg_search", h, q, K, 128))
+    finally:
+        lib().fg_index_free(h)
