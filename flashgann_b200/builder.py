@@ -100,6 +100,7 @@ class DatasetSpec:
     kind: str = "int_gmm"      # int_gmm | int_gmm_dup | norm_aniso | lowrank
     knn_k: int = 64
     gt_k: int = 100
+    knn: str = "exact"         # graph candidates: exact | exact_tf32 | partitioned (see build_graph)
 
 
 SPECS = {
@@ -115,6 +116,14 @@ SPECS = {
     # BASELINE.json configs[3] (1M x 1536, L2-normalised low-rank) at a fifth of the base size
     "c4s_200k": DatasetSpec("c4s_200k", 200_000, 1_000, 1536, 1, 0.0, 0.0, 0.0, 32, 100,
                             (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=4, kind="lowrank"),
+    # BASELINE.json configs[2] at full size: 10M x 96, L2-normalised anisotropic mixture
+    "c3_10m": DatasetSpec("c3_10m", 10_000_000, 10_000, 96, 1000, 0.0, 0.0, 0.0, 32, 100,
+                          (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=3, kind="norm_aniso",
+                          knn="partitioned"),
+    # BASELINE.json configs[3] at full size: 1M x 1536, L2-normalised low-rank model
+    "c4_1m": DatasetSpec("c4_1m", 1_000_000, 1_000, 1536, 1, 0.0, 0.0, 0.0, 32, 100,
+                         (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=4, kind="lowrank",
+                         knn="exact_tf32"),
     # the headline config's per-component structure (5,000 points per component, degree 32)
     # at a fifth of the size, for profiling captures that must stay small
     "p_200k": DatasetSpec("p_200k", 200_000, 2_000, 128, 40, 25.0, 0.0, 255.0, 32, 100,
@@ -191,9 +200,14 @@ def _draw(spec: DatasetSpec, stream: int, m: int) -> np.ndarray:
         def draw(stream: int, m: int) -> np.ndarray:
             r = _rng(spec.seed, stream)
             lab = r.integers(0, spec.n_comp, size=m)
-            v = centres[lab] + r.standard_normal((m, spec.dim)) * scales[lab]
-            v /= np.linalg.norm(v, axis=1, keepdims=True)
-            return v.astype(np.float32)
+            out = np.empty((m, spec.dim), dtype=np.float32)
+            step = 1 << 18  # rows per chunk (the stream's values do not depend on the chunking)
+            for s0 in range(0, m, step):
+                e = min(m, s0 + step)
+                v = centres[lab[s0:e]] + r.standard_normal((e - s0, spec.dim)) * scales[lab[s0:e]]
+                v /= np.linalg.norm(v, axis=1, keepdims=True)
+                out[s0:e] = v
+            return out
 
         return draw(stream, m)
     if spec.kind == "int_gmm_dup":
@@ -247,11 +261,13 @@ def _is_integer_data(x: np.ndarray) -> bool:
 
 
 def brute_force_knn(base: np.ndarray, queries: Optional[np.ndarray], k: int, device=None,
-                    exclude_self: bool = False, chunk: int = 0) -> Tuple[np.ndarray, np.ndarray]:
+                    exclude_self: bool = False, chunk: int = 0, tf32: bool = False) -> Tuple[np.ndarray, np.ndarray]:
     """Exact k nearest neighbours by squared L2, ties broken by smaller id.
 
     Integer-valued data (|x| <= 255, the BASELINE integer configs) is searched
-    with exact integer distances; float data with fp32 distances.
+    with exact integer distances; float data with fp32 distances (tf32: the
+    selection's products in TF32 on tensor cores -- graph construction only,
+    the selected rows are still ranked by float64 distances).
     Returns (ids int64 [m, k], d2 float64 [m, k]) sorted ascending.
     """
     dev = _device(device)
@@ -265,9 +281,18 @@ def brute_force_knn(base: np.ndarray, queries: Optional[np.ndarray], k: int, dev
     if chunk <= 0:
         budget = (6 << 30) if dev.type == "cuda" else (1 << 29)
         chunk = max(16, min(m, budget // max(1, n * 12)))
+    idx_all = torch.arange(n, device=dev, dtype=torch.int64)
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = bool(tf32 and not exact)
+    try:
+        return _brute_chunks(xb, xq, nb, nqv, idx_all, k, m, n, chunk, exact, exclude_self, shift, dev)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+
+
+def _brute_chunks(xb, xq, nb, nqv, idx_all, k, m, n, chunk, exact, exclude_self, shift, dev):
     ids_out = np.empty((m, k), dtype=np.int64)
     d_out = np.empty((m, k), dtype=np.float64)
-    idx_all = torch.arange(n, device=dev, dtype=torch.int64)
     for s in range(0, m, chunk):
         e = min(m, s + chunk)
         d = nqv[s:e, None] + nb[None, :] - 2.0 * (xq[s:e] @ xb.T)
@@ -295,6 +320,87 @@ def brute_force_knn(base: np.ndarray, queries: Optional[np.ndarray], k: int, dev
         ids_out[s:e] = torch.gather(ids, 1, order).cpu().numpy()
         d_out[s:e] = torch.gather(dd, 1, order).cpu().numpy()
     return ids_out, d_out
+
+
+def _nearest_centroid(x: torch.Tensor, cent: torch.Tensor, chunk: int = 1 << 18) -> torch.Tensor:
+    """Index of the nearest centroid (squared L2) of every row of x."""
+    cn = (cent * cent).sum(1)
+    out = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
+    for s in range(0, x.shape[0], chunk):
+        xs = x[s:s + chunk]
+        out[s:s + chunk] = torch.argmin(cn[None, :] - 2.0 * (xs @ cent.T), dim=1)
+    return out
+
+
+def partitioned_knn(x: np.ndarray, k: int, seed: int, device=None, cluster_size: int = 2048, probe: int = 8,
+                    kmeans_iters: int = 10, verbose: bool = False) -> Tuple[np.ndarray, np.ndarray]:
+    """Approximate k nearest neighbours of every row of x (itself excluded),
+    for bases too large for the exact search: k-means (on a seeded sample,
+    centroid sums formed on the host so the result is deterministic) splits
+    the rows into clusters of about `cluster_size`; the neighbours of a row
+    are the exact k nearest among the members of the `probe` clusters whose
+    centroids lie nearest its own cluster's centroid (its own included).
+    Returns (ids int64 [n, k], d2 float64 [n, k]) ascending, -1 / inf where a
+    row's clusters hold fewer than k other rows."""
+    import time
+    t0 = time.time()
+    dev = _device(device)
+    n, dim = x.shape
+    xt = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(dev)
+    norms = (xt * xt).sum(1)
+    C = max(1, n // cluster_size)
+    rg = _rng(seed, 11)
+    m = min(n, 64 * C)
+    sample_idx = np.sort(rg.choice(n, size=m, replace=False))
+    sample_h = np.ascontiguousarray(x[sample_idx], dtype=np.float32)
+    sample = torch.from_numpy(sample_h).to(dev)
+    cent_h = sample_h[rg.choice(m, size=C, replace=False)].astype(np.float64)
+    for _ in range(kmeans_iters):
+        lab = _nearest_centroid(sample, torch.from_numpy(cent_h.astype(np.float32)).to(dev)).cpu().numpy()
+        order = np.argsort(lab, kind="stable")
+        lab_s = lab[order]
+        cuts = np.flatnonzero(np.diff(lab_s)) + 1
+        first = np.concatenate([[0], cuts])
+        sums = np.add.reduceat(sample_h[order].astype(np.float64), first, axis=0)
+        cnt = np.diff(np.concatenate([first, [m]]))
+        cent_h[lab_s[first]] = sums / cnt[:, None]
+    cent = torch.from_numpy(cent_h.astype(np.float32)).to(dev)
+    labels = _nearest_centroid(xt, cent)
+    members = torch.argsort(labels, stable=True)
+    counts = torch.bincount(labels, minlength=C)
+    starts = torch.cumsum(counts, 0) - counts
+    cc = (cent * cent).sum(1)
+    cd = cc[:, None] + cc[None, :] - 2.0 * (cent @ cent.T)
+    cd.fill_diagonal_(-1.0)  # a cluster always probes itself first
+    nbr = torch.topk(cd, min(probe, C), dim=1, largest=False).indices.cpu().numpy()
+    counts_h, starts_h = counts.cpu().numpy(), starts.cpu().numpy()
+    if verbose:
+        print(f"[builder] partitioned k-NN: {C} clusters (sizes {counts_h.min()}..{counts_h.max()}), "
+              f"{time.time() - t0:.1f}s", flush=True)
+    out_i = torch.full((n, k), -1, dtype=torch.int64, device=dev)
+    out_d = torch.full((n, k), float("inf"), dtype=torch.float32, device=dev)
+    for c in range(C):
+        if counts_h[c] == 0:
+            continue
+        q = members[starts_h[c]:starts_h[c] + counts_h[c]]
+        pool = torch.cat([members[starts_h[j]:starts_h[j] + counts_h[j]] for j in nbr[c]])
+        d = norms[q][:, None] + norms[pool][None, :] - 2.0 * (xt[q] @ xt[pool].T)
+        d.masked_fill_(q[:, None] == pool[None, :], float("inf"))
+        kk = min(k, pool.numel() - 1)
+        if kk <= 0:
+            continue
+        dv, di = torch.topk(d, kk, dim=1, largest=False, sorted=True)
+        nb = pool[di]
+        # distances recomputed as sums of squared differences: symmetric bit
+        # for bit, so a pair's forward and reverse edges carry one value
+        dx = ((xt[q][:, None, :] - xt[nb]) ** 2).sum(-1)
+        dx, o = torch.sort(dx, dim=1, stable=True)
+        nb = torch.gather(nb, 1, o)
+        out_i[q, :kk] = torch.where(torch.isinf(torch.gather(dv, 1, o)), torch.full_like(nb, -1), nb)
+        out_d[q, :kk] = dx
+    if verbose:
+        print(f"[builder] partitioned k-NN done, {time.time() - t0:.1f}s", flush=True)
+    return out_i.cpu().numpy(), out_d.double().cpu().numpy()
 
 
 # --------------------------------------------------------------------------
@@ -331,6 +437,50 @@ def _merge_reverse(ids: np.ndarray, d: np.ndarray, cap: int, device) -> Tuple[np
     return out_i.cpu().numpy(), out_d.cpu().numpy()
 
 
+def _merge_reverse_large(ids: np.ndarray, d: np.ndarray, cap: int, device) -> Tuple[np.ndarray, np.ndarray]:
+    """_merge_reverse for bases of millions of rows: the same lists (nearest
+    `cap` of the forward and reverse k-NN edges per node, ordered by
+    (distance, id)), with 32-bit node ids and float32 distances on the
+    device and two stable sorts instead of three, which keeps ten million
+    nodes' 1.3 billion edges within a few tens of GB.  Needs symmetric
+    distances (d(u, v) == d(v, u) bit for bit)."""
+    dev = _device(device)
+    n, k = ids.shape
+    src = torch.arange(n, device=dev, dtype=torch.int32).repeat_interleave(k)
+    dst = torch.from_numpy(ids.reshape(-1)).to(dev)
+    dd = torch.from_numpy(d.reshape(-1).astype(np.float32)).to(dev)
+    ok = dst >= 0
+    src, dst, dd = src[ok], dst[ok].to(torch.int32), dd[ok]
+    node = torch.cat([src, dst])
+    cand = torch.cat([dst, src])
+    dist = torch.cat([dd, dd])
+    del src, dst, dd, ok
+    o = torch.argsort(cand, stable=True)
+    node, cand, dist = node[o], cand[o], dist[o]
+    del o
+    # (node, distance) as one 64-bit key: distances are >= 0, so their float
+    # bits order like the values
+    key = (node.to(torch.int64) << 32) | (dist.view(torch.int32).to(torch.int64) & 0xFFFFFFFF)
+    o = torch.argsort(key, stable=True)
+    del key
+    node, cand, dist = node[o], cand[o], dist[o]
+    del o
+    keep = torch.ones_like(node, dtype=torch.bool)
+    keep[1:] = (node[1:] != node[:-1]) | (cand[1:] != cand[:-1])
+    node, cand, dist = node[keep], cand[keep], dist[keep]
+    del keep
+    counts = torch.bincount(node, minlength=n)
+    starts = torch.cumsum(counts, 0) - counts
+    rank = torch.arange(node.numel(), device=dev) - starts[node.long()]
+    sel = rank < cap
+    out_i = torch.full((n, cap), -1, dtype=torch.int64, device=dev)
+    out_d = torch.full((n, cap), float("inf"), dtype=torch.float64, device=dev)
+    nl = node[sel].long()
+    out_i[nl, rank[sel]] = cand[sel].long()
+    out_d[nl, rank[sel]] = dist[sel].double()
+    return out_i.cpu().numpy(), out_d.cpu().numpy()
+
+
 def rng_prune(x: np.ndarray, cand: np.ndarray, cand_d: np.ndarray, R: int, alpha: float = 1.0,
               device=None, batch: int = 0) -> np.ndarray:
     """Relative-neighbourhood pruning of sorted candidate lists.
@@ -343,6 +493,9 @@ def rng_prune(x: np.ndarray, cand: np.ndarray, cand_d: np.ndarray, R: int, alpha
     n, C = cand.shape
     if batch <= 0:
         batch = 8192 if dev.type == "cuda" else 1024
+        if dev.type == "cuda" and n > 2_000_000:
+            # large bases: ~4 GB of gathered rows and pair distances per batch
+            batch = int(min(32768, max(1024, (4 << 30) // (C * (x.shape[1] + C) * 8))))
     xt = torch.from_numpy(np.ascontiguousarray(x)).to(dev)
     out = np.full((n, R), -1, dtype=np.int64)
     a2 = alpha * alpha
@@ -376,22 +529,38 @@ def rng_prune(x: np.ndarray, cand: np.ndarray, cand_d: np.ndarray, R: int, alpha
 
 
 def build_graph(x: np.ndarray, degree: int, seed: int, knn_k: int = 64, device=None,
-                random_links: Optional[int] = None) -> Tuple[np.ndarray, int]:
+                random_links: Optional[int] = None, knn: str = "exact",
+                verbose: bool = False) -> Tuple[np.ndarray, int]:
     """Degree-`degree` neighbour lists (int64, -1 = empty) and an entry point.
 
     Every node keeps `degree - r` relative-neighbourhood-pruned local edges and
     `r` seeded uniformly random long edges (r = max(2, degree // 8)); the
     entry point (the node nearest the centroid) spends half of its slots on
     random long edges.  Without long edges a single entry point never leaves
-    its own component of a well-separated mixture.
+    its own component of a well-separated mixture.  knn = "exact" takes the
+    candidates from the brute-force k-NN, "partitioned" from
+    partitioned_knn (bases of millions of rows), "exact_tf32" from the
+    brute force with TF32 products (high-dimensional bases).
     """
     n = x.shape[0]
     k = min(knn_k, n - 1)
     r = max(2, degree // 8) if random_links is None else random_links
     r = min(r, degree - 1)
-    ids, d = brute_force_knn(x, None, k, device=device, exclude_self=True)
-    cand, cand_d = _merge_reverse(ids, d, cap=min(n - 1, max(96, int(1.5 * k))), device=device)
+    if knn in ("exact", "exact_tf32"):
+        ids, d = brute_force_knn(x, None, k, device=device, exclude_self=True, tf32=knn == "exact_tf32")
+    elif knn == "partitioned":
+        ids, d = partitioned_knn(x, k, seed, device=device, verbose=verbose)
+    else:
+        raise ValueError(f"unknown k-NN method {knn!r}")
+    if verbose:
+        print(f"[builder] k-NN ({knn}) done", flush=True)
+    merge = _merge_reverse if knn == "exact" or n <= 2_000_000 else _merge_reverse_large
+    cand, cand_d = merge(ids, d, cap=min(n - 1, max(96, int(1.5 * k))), device=device)
+    if verbose:
+        print("[builder] reverse edges merged", flush=True)
     local = rng_prune(x, cand, cand_d, degree - r, device=device)
+    if verbose:
+        print("[builder] pruned", flush=True)
     rg = _rng(seed, 5)
     rand = (np.arange(n)[:, None] + 1 + rg.integers(0, max(1, n - 1), size=(n, r))) % n
     nbrs = np.concatenate([local, rand], axis=1)
@@ -505,11 +674,14 @@ def write_codebook(path: str, entry: int, rows: np.ndarray, signs: np.ndarray) -
 
 
 def read_codebook(path: str, n: int, dim: int, degree: int) -> Tuple[int, np.ndarray, np.ndarray]:
+    """(entry point, rows [n, row] float32, signs [D]); the rows are a
+    read-only memory map of the file (codebooks of tens of GB)."""
     L = layout(dim, degree)
     with open(path, "rb") as f:
         entry = struct.unpack("<I", f.read(4))[0]
-        rows = np.fromfile(f, dtype=np.float32, count=n * L.row).reshape(n, L.row)
+        f.seek(4 + n * L.row * 4)
         signs = np.fromfile(f, dtype=np.float32, count=L.padded_dim)
+    rows = np.memmap(path, dtype=np.float32, mode="r", offset=4, shape=(n, L.row))
     return entry, rows, signs
 
 
@@ -583,7 +755,8 @@ def materialize(name_or_spec, cache_dir: Optional[str] = None, device=None,
     base, queries = generate_vectors(spec)
     if verbose:
         print(f"[builder] {spec.name}: vectors {time.time() - t0:.1f}s", flush=True)
-    nbrs, entry = build_graph(base, spec.degree, spec.seed, knn_k=spec.knn_k, device=device)
+    nbrs, entry = build_graph(base, spec.degree, spec.seed, knn_k=spec.knn_k, device=device, knn=spec.knn,
+                              verbose=verbose)
     if verbose:
         print(f"[builder] {spec.name}: graph {time.time() - t0:.1f}s", flush=True)
     signs = make_signs(L.padded_dim, spec.seed)
