@@ -47,6 +47,7 @@ struct SearchPlan {
     uint32_t slots = 0;        // warp kernel: visited-set slots
     size_t slice_bytes = 0;    // warp kernel: shared memory per query
     int min_ctas = 0;          // warp kernel: CTAs per SM its register budget is compiled for
+    uint32_t blk = 0;          // warp kernel, staged variant: bytes of one parent block (0: not staged)
     size_t smem_bytes = 0;
     int grid = 0;
     int threads = 0;
@@ -58,7 +59,7 @@ cudaError_t launch_search(const SearchArgs& a, const SearchPlan& plan, cudaStrea
 
 // The warp-per-query kernel (fg_search_warp.cu): padded dimensions 32..256.
 bool warp_kernel_supports(int padded_dim);
-int plan_search_warp(const SearchArgs& a, SearchPlan* plan, int device, char* err, size_t errlen);
+int plan_search_warp(const SearchArgs& a, SearchPlan* plan, int device, char* err, size_t errlen, bool staged);
 cudaError_t launch_search_warp(const SearchArgs& a, const SearchPlan& plan, cudaStream_t stream);
 
 cudaError_t launch_query_prepare(const float* queries, int nq, int dim, const float* signs, float* rotated,

@@ -734,14 +734,18 @@ int variant_from_env() {
 // Kernel choice where both apply (padded dim <= 256; they return identical
 // results): the warp kernel for batches of more than 4 queries per SM, where
 // its 20 resident queries per SM pay; below that the CTA kernel's 8 warps per
-// query finish sooner.  FG_KERNEL=warp or FG_KERNEL=cta forces one.
-bool use_warp_kernel(int nq, int device) {
+// query finish sooner.  FG_KERNEL=warp, =staged (the warp kernel's staged
+// variant) or =cta forces one.
+enum class Choice { kCta, kWarp, kStaged };
+
+Choice kernel_choice(int nq, int device) {
     const char* v = getenv("FG_KERNEL");
-    if (v && v[0] == 'c') return false;
-    if (v && v[0] == 'w') return true;
+    if (v && v[0] == 'c') return Choice::kCta;
+    if (v && v[0] == 'w') return Choice::kWarp;
+    if (v && v[0] == 's') return Choice::kStaged;
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) sms = 148;
-    return nq > 4 * sms;
+    return nq > 4 * sms ? Choice::kWarp : Choice::kCta;
 }
 
 int merge_width(uint32_t itopk) {
@@ -815,7 +819,10 @@ int plan_search(const SearchArgs& a, SearchPlan* p, int device, char* err, size_
     p->mp_active = merge_active(p->padded);
     const uintptr_t base = reinterpret_cast<uintptr_t>(a.rows);
     p->vec_codes = ((base % 16) == 0 && ((a.row * 4) % 16) == 0 && ((a.code_off * 4) % 16) == 0) ? 1 : 0;
-    if (warp_kernel_supports(a.padded_dim) && use_warp_kernel(a.nq, device)) return plan_search_warp(a, p, device, err, errlen);
+    if (warp_kernel_supports(a.padded_dim)) {
+        const Choice c = kernel_choice(a.nq, device);
+        if (c != Choice::kCta) return plan_search_warp(a, p, device, err, errlen, c == Choice::kStaged);
+    }
     p->kernel = 0;
     p->variant = variant_from_env();
     const int nw = kVariants[p->variant].nw;

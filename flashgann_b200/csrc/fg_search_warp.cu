@@ -53,6 +53,12 @@ constexpr int kWarpsPerCta = 4;  // largest CTA; the planner may launch 1 or 2 w
 // query slices of 5 CTAs fit the SM's shared memory, 5 (96 registers).
 constexpr int kCtasLarge = 4;
 constexpr int kCtasSmall = 5;
+// The staged variant (3 CTAs per SM, 168 registers): every parent block of a
+// speculative iteration is copied into a shared-memory ring with cp.async at
+// once, instead of one block ahead in registers, and exact distances run 16
+// rows per round.  It shortens each query's dependent chain of loads and is
+// the planner's choice for batches that leave most warp slots idle.
+constexpr int kCtasStaged = 3;
 
 struct WPlan {
     uint32_t padded, cbs, collect_cap;
@@ -61,6 +67,7 @@ struct WPlan {
     int max_iter;
     int mp_active;
     uint32_t slice;  // shared-memory bytes per warp
+    uint32_t blk;    // staged variant: bytes of a parent block (codes, factors, ids), a multiple of 16
 };
 
 // One warp's slice of the CTA's dynamic shared memory.
@@ -77,6 +84,7 @@ struct WSlice {
     uint32_t* eslot;  // single-expander path: candidate slot of each evaluation
     uint32_t* pnode;  // expanders of the iteration
     float* pdist;
+    unsigned char* ring;  // staged variant: SEARCH_WIDTH parent blocks
     // stage and eslot (256 contiguous bytes) double as the merge's tie fix-up
     // list, and stage as the query factors during set-up
     QueryState* qs;
@@ -85,7 +93,7 @@ struct WSlice {
 __host__ __device__ inline size_t a16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
 
 __host__ __device__ inline size_t slice_layout(uint32_t padded, uint32_t slots, int D, bool mp, WSlice* s,
-                                               unsigned char* base) {
+                                               unsigned char* base, size_t ring_bytes = 0) {
     size_t off = 0;
     auto take = [&](size_t bytes) {
         unsigned char* p = base ? base + off : nullptr;
@@ -106,6 +114,7 @@ __host__ __device__ inline size_t slice_layout(uint32_t padded, uint32_t slots, 
     p = take(32 * 4); if (s) s->eslot = reinterpret_cast<uint32_t*>(p);
     p = take(SEARCH_WIDTH * 4); if (s) s->pnode = reinterpret_cast<uint32_t*>(p);
     p = take(SEARCH_WIDTH * 4); if (s) s->pdist = reinterpret_cast<float*>(p);
+    p = ring_bytes ? take(ring_bytes) : nullptr; if (s) s->ring = p;
     if (s) s->qs = reinterpret_cast<QueryState*>(s->stage);
     (void)mp;
     return off;
@@ -220,6 +229,63 @@ __device__ __forceinline__ uint4 ldg_pinned_v4(const void* p) {
     uint4 v;
     asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
+}
+
+// 16-byte global -> shared copies that complete asynchronously (cp.async,
+// L2 only), grouped per parent; wait_groups(n) returns once at most n of the
+// calling lane's groups are still in flight.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async_wait_groups(int n) {
+    switch (n) {
+        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+        case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+        case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+    }
+}
+
+// The staged block of parent t (codes | triple_x | f_dq | f_vq | ids, as in
+// the codebook row) into lane `lane`'s ParentLane, from shared memory.
+template <int W>
+__device__ __forceinline__ void parent_from_ring(const unsigned char* blk, int deg, int D, int lane, ParentLane<W>& p) {
+    const int cbytes = deg * (D / 8);
+    const float* fac = reinterpret_cast<const float*>(blk + cbytes);
+    p.child = kMax;
+    p.tx = FLT_MAX;
+    p.fdq = 0.0f;
+    p.fvq = 0.0f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) p.c[w] = 0;
+    if (lane < deg) {
+        p.child = reinterpret_cast<const uint32_t*>(fac + 3 * deg)[lane];
+        p.tx = fac[lane];
+        p.fdq = fac[deg + lane];
+        p.fvq = fac[2 * deg + lane];
+        const uint32_t* code = reinterpret_cast<const uint32_t*>(blk) + static_cast<size_t>(lane) * W;
+        if constexpr (W % 4 == 0) {
+#pragma unroll
+            for (int w = 0; w < W; w += 4) {
+                const uint4 x = *reinterpret_cast<const uint4*>(code + w);
+                p.c[w] = x.x;
+                p.c[w + 1] = x.y;
+                p.c[w + 2] = x.z;
+                p.c[w + 3] = x.w;
+            }
+        } else {
+#pragma unroll
+            for (int w = 0; w < W; ++w) p.c[w] = code[w];
+        }
+    }
 }
 
 // load_parent (fg_device.cuh) with pinned loads: neighbour id, the three
@@ -692,11 +758,11 @@ __device__ __noinline__ void restore_visited(uint32_t* hash, const uint32_t* bid
     __syncwarp();
 }
 
-template <int W, int MERGE, bool IP>
+template <int W, int MERGE, bool IP, bool STAGED>
 __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& pl, const WSlice& s,
                                              const uint16_t* bnd, uint32_t qid, bool vec, int lane) {
     constexpr bool mp = MERGE == 0;
-    constexpr int G = 8;  // rows per exact-distance round
+    constexpr int G = STAGED && W <= 4 ? 16 : 8;  // rows per exact-distance round
     const int dim = a.dim, deg = a.degree, beam = a.beam;
     const uint32_t P = pl.padded, cbs = pl.cbs, slots = pl.slots;
     const float* __restrict__ rows = a.rows;
@@ -911,16 +977,35 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
             const int keep0 = keep_for(active, th, rho, false, 0);
             // keep_for(active, th, rho, cut, near) = clamp(cut ? clamp(near, 1, cap) : cap, 1, active)
             const int cap = keep_cap(active, th, rho);
-            // one parent per step; the next parent's block is loaded while
-            // this one is examined (the last step reloads its own block)
             ParentLane<W> cur;
-            load_parent_pinned<W>(rows + static_cast<uint64_t>(s.pnode[0]) * rowf, a, deg, vec, lane, cur);
+            if constexpr (STAGED) {
+                // every parent's block in flight at once: one cp.async group
+                // per parent into its ring slot (blocks are 16-byte aligned)
+                const uint32_t chunks = pl.blk >> 4;
+                for (uint32_t t = 0; t < num; ++t) {
+                    const unsigned char* src = reinterpret_cast<const unsigned char*>(
+                        rows + static_cast<uint64_t>(s.pnode[t]) * rowf + a.code_off);
+                    unsigned char* dst = s.ring + t * pl.blk;
+                    for (uint32_t c = static_cast<uint32_t>(lane); c < chunks; c += 32) cp_async16(dst + 16 * c, src + 16 * c);
+                    cp_async_commit();
+                }
+            } else {
+                // one parent per step; the next parent's block is loaded while
+                // this one is examined (the last step reloads its own block)
+                load_parent_pinned<W>(rows + static_cast<uint64_t>(s.pnode[0]) * rowf, a, deg, vec, lane, cur);
+            }
             uint32_t total = 0;
 #pragma unroll 1
             for (int t = 0; t < static_cast<int>(num); ++t) {
-                const int tn = t + 1 < static_cast<int>(num) ? t + 1 : t;
                 ParentLane<W> nxt;
-                load_parent_pinned<W>(rows + static_cast<uint64_t>(s.pnode[tn]) * rowf, a, deg, vec, lane, nxt);
+                if constexpr (STAGED) {
+                    cp_async_wait_groups(static_cast<int>(num) - 1 - t);
+                    __syncwarp();
+                    parent_from_ring<W>(s.ring + t * pl.blk, deg, 32 * W, lane, cur);
+                } else {
+                    const int tn = t + 1 < static_cast<int>(num) ? t + 1 : t;
+                    load_parent_pinned<W>(rows + static_cast<uint64_t>(s.pnode[tn]) * rowf, a, deg, vec, lane, nxt);
+                }
                 const uint32_t child = cur.child;
                 bool valid = child != kMax && child < a.n && !w_contains(s.hash, slots, child);
                 const uint32_t raw_valid = __popc(__ballot_sync(kFull, valid));
@@ -956,7 +1041,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
                     prefetch_row(rows + static_cast<uint64_t>(child) * rowf, dim);
                 }
                 total += __popc(kb);
-                cur = nxt;
+                if constexpr (!STAGED) cur = nxt;
             }
             __syncwarp();
             // inserts and compaction in (parent, rank) order; a child kept by
@@ -1007,6 +1092,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
 template <int W, int MERGE, bool IP, int MINB>
 __global__ void __launch_bounds__(kWarpsPerCta * 32, MINB) search_warp_kernel(const SearchArgs a, const WPlan pl,
                                                                                   int vec_codes) {
+    constexpr bool kStaged = MINB == kCtasStaged;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     // merge-path output segment boundaries s * itopk / active (launch constants)
     __shared__ uint16_t bnd[MERGE == 0 ? BLOCK_SIZE + 1 : 1];
@@ -1017,13 +1103,14 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, MINB) search_warp_kernel(co
     __syncthreads();  // the only block barrier: the warps are independent from here on
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     WSlice s;
-    slice_layout(pl.padded, pl.slots, 32 * W, MERGE == 0, &s, smem_raw + static_cast<size_t>(warp) * pl.slice);
+    slice_layout(pl.padded, pl.slots, 32 * W, MERGE == 0, &s, smem_raw + static_cast<size_t>(warp) * pl.slice,
+                 kStaged ? static_cast<size_t>(SEARCH_WIDTH) * pl.blk : 0);
     for (;;) {
         uint32_t qid = 0;
         if (lane == 0) qid = atomicAdd(a.work_counter, 1u);
         qid = __shfl_sync(kFull, qid, 0);
         if (qid >= static_cast<uint32_t>(a.nq)) break;
-        search_query<W, MERGE, IP>(a, pl, s, bnd, qid, vec_codes != 0, lane);
+        search_query<W, MERGE, IP, kStaged>(a, pl, s, bnd, qid, vec_codes != 0, lane);
     }
 }
 
@@ -1047,9 +1134,11 @@ const void* pick_w(int W, int merge) {
     }
 }
 
-// kernel for W = padded dim / 32, the beam merge, the metric and the register budget
+// kernel for W = padded dim / 32, the beam merge, the metric and the register
+// budget (kCtasStaged: the staged variant)
 const void* warp_kernel_for(int W, int merge, bool ip, int minb) {
     if (minb == kCtasSmall) return ip ? pick_w<true, kCtasSmall>(W, merge) : pick_w<false, kCtasSmall>(W, merge);
+    if (minb == kCtasStaged) return ip ? pick_w<true, kCtasStaged>(W, merge) : pick_w<false, kCtasStaged>(W, merge);
     return ip ? pick_w<true, kCtasLarge>(W, merge) : pick_w<false, kCtasLarge>(W, merge);
 }
 
@@ -1057,7 +1146,17 @@ const void* warp_kernel_for(int W, int merge, bool ip, int minb) {
 
 bool warp_kernel_supports(int padded_dim) { return padded_dim >= 32 && padded_dim <= 256; }
 
-int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, size_t errlen) {
+// Bytes of a parent's expansion block (codes, three factors, ids); the staged
+// variant needs it 16-byte aligned and a multiple of 16 bytes.
+static uint32_t parent_block_bytes(const SearchArgs& a) {
+    return static_cast<uint32_t>(a.degree) * static_cast<uint32_t>(a.padded_dim / 8 + 16);
+}
+
+bool warp_staged_supported(const SearchArgs& a, const SearchPlan& p) {
+    return p.vec_codes && (parent_block_bytes(a) % 16) == 0;
+}
+
+int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, size_t errlen, bool staged) {
     const int D = a.padded_dim;
     uint32_t req = p->padded + p->cbs * SMALL_HASH_RESET_INTERVAL;
     uint32_t slots = req + (req + 11) / 12;  // ~93 % at the bound (two-choice buckets)
@@ -1067,7 +1166,10 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
     slots = (slots + 31) & ~31u;
     p->kernel = 1;
     p->slots = slots;
-    p->slice_bytes = slice_layout(p->padded, slots, D, p->merge_n2 == 0, nullptr, nullptr);
+    staged = staged && warp_staged_supported(a, *p);
+    p->blk = staged ? parent_block_bytes(a) : 0;
+    p->slice_bytes = slice_layout(p->padded, slots, D, p->merge_n2 == 0, nullptr, nullptr,
+                                  static_cast<size_t>(SEARCH_WIDTH) * p->blk);
     int sms = 0, max_smem = 0;
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
@@ -1084,7 +1186,9 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
     // go to the larger CTA
     const void* best = nullptr;
     int best_q = 0;
-    for (int minb : {kCtasSmall, kCtasLarge}) {
+    const int budgets[2] = {staged ? kCtasStaged : kCtasSmall, staged ? kCtasStaged : kCtasLarge};
+    for (int bi = 0; bi < (staged ? 1 : 2); ++bi) {
+        const int minb = budgets[bi];
         const void* fn = warp_kernel_for(D / 32, p->merge_n2, a.use_ip != 0, minb);
         for (int wpc : {kWarpsPerCta, 2, 1}) {
             const size_t smem = p->slice_bytes * static_cast<size_t>(wpc);
@@ -1135,6 +1239,7 @@ cudaError_t launch_search_warp(const SearchArgs& a, const SearchPlan& p, cudaStr
     pl.max_iter = p.max_iter;
     pl.mp_active = p.mp_active;
     pl.slice = static_cast<uint32_t>(p.slice_bytes);
+    pl.blk = p.blk;
     cudaError_t e = cudaMemsetAsync(a.work_counter, 0, sizeof(uint32_t), stream);
     if (e != cudaSuccess) return e;
     const void* fn = warp_kernel_for(a.padded_dim / 32, p.merge_n2, a.use_ip != 0, p.min_ctas);

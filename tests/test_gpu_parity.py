@@ -54,9 +54,11 @@ def _run_gpu(qg, queries, K, beam, trace_cap=0):
     return out
 
 
-@pytest.fixture(params=["warp", "cta"])
+@pytest.fixture(params=["warp", "staged", "cta"])
 def kernel(request, monkeypatch):
-    """Both search kernels (the planner picks by batch size; FG_KERNEL forces one)."""
+    """Every search kernel: the warp kernel, its staged variant (parent blocks
+    copied to shared memory with cp.async) and the CTA kernel (the planner
+    picks by batch size; FG_KERNEL forces one)."""
     monkeypatch.setenv("FG_KERNEL", request.param)
     return request.param
 
