@@ -48,6 +48,8 @@ struct SearchPlan {
     size_t slice_bytes = 0;    // warp kernel: shared memory per query
     int min_ctas = 0;          // warp kernel: CTAs per SM its register budget is compiled for
     uint32_t blk = 0;          // warp kernel, staged variant: bytes of one parent block (0: not staged)
+    int warp_mode = 0;         // warp kernel: 0 one warp per query, 1 staged, 2 a pair of warps per query
+    int resident_queries = 0;  // warp kernel: queries resident at once on the device
     size_t smem_bytes = 0;
     int grid = 0;
     int threads = 0;
@@ -59,7 +61,8 @@ cudaError_t launch_search(const SearchArgs& a, const SearchPlan& plan, cudaStrea
 
 // The warp-per-query kernel (fg_search_warp.cu): padded dimensions 32..256.
 bool warp_kernel_supports(int padded_dim);
-int plan_search_warp(const SearchArgs& a, SearchPlan* plan, int device, char* err, size_t errlen, bool staged);
+// mode: 0 one warp per query, 1 its staged variant, 2 a pair of warps per query
+int plan_search_warp(const SearchArgs& a, SearchPlan* plan, int device, char* err, size_t errlen, int mode);
 cudaError_t launch_search_warp(const SearchArgs& a, const SearchPlan& plan, cudaStream_t stream);
 
 cudaError_t launch_query_prepare(const float* queries, int nq, int dim, const float* signs, float* rotated,

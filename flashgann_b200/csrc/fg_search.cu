@@ -736,13 +736,14 @@ int variant_from_env() {
 // its 20 resident queries per SM pay; below that the CTA kernel's 8 warps per
 // query finish sooner.  FG_KERNEL=warp, =staged (the warp kernel's staged
 // variant) or =cta forces one.
-enum class Choice { kCta, kWarp, kStaged };
+enum class Choice { kCta, kWarp, kStaged, kPair };
 
 Choice kernel_choice(int nq, int device) {
     const char* v = getenv("FG_KERNEL");
     if (v && v[0] == 'c') return Choice::kCta;
     if (v && v[0] == 'w') return Choice::kWarp;
     if (v && v[0] == 's') return Choice::kStaged;
+    if (v && v[0] == 'p') return Choice::kPair;
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) sms = 148;
     return nq > 4 * sms ? Choice::kWarp : Choice::kCta;
@@ -821,7 +822,8 @@ int plan_search(const SearchArgs& a, SearchPlan* p, int device, char* err, size_
     p->vec_codes = ((base % 16) == 0 && ((a.row * 4) % 16) == 0 && ((a.code_off * 4) % 16) == 0) ? 1 : 0;
     if (warp_kernel_supports(a.padded_dim)) {
         const Choice c = kernel_choice(a.nq, device);
-        if (c != Choice::kCta) return plan_search_warp(a, p, device, err, errlen, c == Choice::kStaged);
+        if (c != Choice::kCta)
+            return plan_search_warp(a, p, device, err, errlen, c == Choice::kStaged ? 1 : c == Choice::kPair ? 2 : 0);
     }
     p->kernel = 0;
     p->variant = variant_from_env();

@@ -59,6 +59,13 @@ constexpr int kCtasSmall = 5;
 // rows per round.  It shortens each query's dependent chain of loads and is
 // the planner's choice for batches that leave most warp slots idle.
 constexpr int kCtasStaged = 3;
+// Kernel modes: one warp per query, the staged variant of it, or a pair of
+// warps per query (the pair mode, for batches that fill few warp slots).
+constexpr int kModeWarp = 0;
+constexpr int kModeStaged = 1;
+constexpr int kModePair = 2;
+// The pair mode's register budget: 4 CTAs of 4 warps (2 queries) per SM.
+constexpr int kCtasPair = 4;
 
 struct WPlan {
     uint32_t padded, cbs, collect_cap;
@@ -408,9 +415,9 @@ __device__ __forceinline__ void eval_round(const float* __restrict__ rows, uint6
 template <int W, int GB, bool IP>
 __device__ __forceinline__ void eval_nodes(const float* __restrict__ rows, uint64_t rowf, int dim, const float (&q)[W],
                                            const uint32_t* nodes, int n, float* out, const uint32_t* slot,
-                                           int lane) {
-    int e0 = 0;
-    for (; e0 < n; e0 += GB) {
+                                           int lane, int first = 0, int stride = GB) {
+    int e0 = first;
+    for (; e0 < n; e0 += stride) {
         uint32_t nd[GB];
 #pragma unroll
         for (int r = 0; r < GB; ++r) nd[r] = nodes[e0 + r < n ? e0 + r : n - 1];
@@ -1089,10 +1096,367 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
     __syncwarp();
 }
 
-template <int W, int MERGE, bool IP, int MINB>
+// ------------------------------------------------------------ pair mode
+// Two warps per query: the leader keeps the query's serial steps (merge,
+// controller, expander pick, compaction and inserts, result write) and both
+// warps split the parallel ones -- the parents of a speculative iteration
+// (the leader takes parents 0, 2, 4, ..., the follower 1, 3, 5, ...) and the
+// exact-distance rounds.  Each parent's kept children go to a list of their
+// own, so the leader's compaction sees them in (parent, rank) order exactly
+// as the one-warp search does, and every visited-set lookup of an iteration
+// still precedes its inserts.  The two warps meet at a named barrier (64
+// threads, id 1 + the pair's index in the CTA) at points both reach on every
+// path: after set-up, after the pick, after the parents, after the
+// compaction, after the distances, and at the end of the query.  Results are
+// the one-warp search's, bit for bit.
+struct PairCtl {
+    QueryState qs;
+    uint32_t qid;
+    int stop;        // the leader found no expander (or hit the iteration limit)
+    int th;
+    float rho;
+    float cutoff;
+    uint32_t num;
+    int ev_n;
+    uint32_t nest_f;  // the follower's estimate count
+    uint32_t kc[SEARCH_WIDTH];  // children kept per parent
+};
+
+// shared bytes after the slice: the control block, then SEARCH_WIDTH lists of 32 ids
+constexpr size_t kPairCtlBytes = (sizeof(PairCtl) + 15) & ~static_cast<size_t>(15);
+constexpr size_t kPairExtraBytes = kPairCtlBytes + static_cast<size_t>(SEARCH_WIDTH) * 32 * 4;
+
+__device__ __forceinline__ void pair_sync(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+
+template <int W, int MERGE, bool IP>
+__device__ __forceinline__ void search_query_pair(const SearchArgs& a, const WPlan& pl, const WSlice& s, PairCtl* ctl,
+                                                  uint32_t* kp, const uint16_t* bnd, uint32_t qid, bool vec, int lane,
+                                                  int role, int bar) {
+    constexpr bool mp = MERGE == 0;
+    constexpr int G = 8;  // rows per exact-distance round
+    const bool lead = role == 0;
+    const int dim = a.dim, deg = a.degree, beam = a.beam;
+    const uint32_t P = pl.padded, cbs = pl.cbs, slots = pl.slots;
+    const float* __restrict__ rows = a.rows;
+    const uint64_t rowf = a.row;
+    uint32_t* bidx = s.bidx;
+    float* bdist = s.bdist;
+
+    // ---------------------------------------------------------------- init
+    const float* q = a.queries + static_cast<size_t>(qid) * dim;
+    float qr[W];
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+        const int d = lane + 32 * k;
+        qr[k] = d < dim ? __ldg(q + d) : 0.0f;
+    }
+    CtlRegs c;
+    c.theta = PHASE1_THETA;
+    c.rho = PHASE1_RHO;
+    c.policy_iters = 0;
+    c.top1 = kMax;
+    c.stall = 0;
+    c.warmup_done = false;
+    c.entry_d = FLT_MAX;
+    c.last_d = FLT_MAX;
+    c.cur_d = FLT_MAX;
+    c.scan = 0;
+    if (lead) {
+        float* qv = reinterpret_cast<float*>(s.hash);
+        uint8_t* quant = reinterpret_cast<uint8_t*>(qv + ((dim + 3) & ~3));
+        for (int i = lane; i < dim; i += 32) qv[i] = q[i];
+        __syncwarp();
+        prep_warp<W>(qv, a.signs, dim, quant, nullptr, s.qs, lane);
+        build_planes(quant, 32 * W, s.planes, s.wrap, s.qs, lane);
+        __syncwarp();
+        if (lane == 0) ctl->qs = *s.qs;
+        __syncwarp();
+        w_clear(s.hash, slots, lane);
+        for (uint32_t i = lane; i < P; i += 32) {
+            bidx[i] = kMax;
+            bdist[i] = FLT_MAX;
+        }
+        s.cidx[lane] = kMax;
+        s.cdist[lane] = FLT_MAX;
+        __syncwarp();
+        // entry point into candidate slot 0 (src/adaptive_search.cuh:110-118)
+        const float ed = dist_one<W, IP>(rows + static_cast<uint64_t>(a.entry) * rowf, qr, dim, lane);
+        if (lane == 0) {
+            s.cidx[0] = a.entry;
+            s.cdist[0] = ed;
+            w_insert(s.hash, slots, a.entry);
+        }
+        __syncwarp();
+        c.entry_d = ed;
+    }
+    pair_sync(bar);
+    const QueryState qsl = ctl->qs;
+    uint32_t c_iters = 0, c_exp = 0, c_eval = 1, n_est = 0;
+
+    // ---------------------------------------------------------------- loop
+    for (int iter = 0; iter < MAX_ITERATIONS; ++iter) {
+        if (lead && (iter + 1) % SMALL_HASH_RESET_INTERVAL == 0) restore_visited(s.hash, s.bidx, slots, beam, lane);
+        if (iter >= pl.max_iter) break;  // the same on both warps
+
+        if (lead) {
+            // merge the previous iteration's candidates (:142-145)
+            uint32_t p0 = 0;
+            if constexpr (mp) {
+                p0 = merge_path_warp(s, cbs, P, pl.mp_active, bnd, lane);
+            } else {
+                merge_bitonic<MERGE>(bidx, bdist, s.cidx, s.cdist, cbs, iter == 0, lane);
+                for (uint32_t i = static_cast<uint32_t>(beam) + lane; i < P; i += 32) {
+                    bidx[i] = kMax;
+                    bdist[i] = FLT_MAX;
+                }
+                __syncwarp();
+            }
+            ++c_iters;
+            // control (src/adaptive_search.cuh:147-217)
+            const float cutoff = bidx[beam - 1] == kMax ? FLT_MAX : bdist[(a.K < beam ? a.K : beam) - 1];
+            const uint32_t b0 = bidx[0];
+            __syncwarp();
+            s.cidx[lane] = kMax;
+            s.cdist[lane] = FLT_MAX;
+            controller_update(c, b0, iter, pl.phase2_rho);
+            uint32_t start = 0;
+            if constexpr (mp) {
+                if (p0 < c.scan) c.scan = p0;
+                start = c.scan & ~31u;
+            }
+            // pick_expanders (include/utils.cuh:752-787)
+            const uint32_t theta = static_cast<uint32_t>(c.theta);
+            uint32_t num = 0, last_pick = 0;
+            const uint32_t lim = (static_cast<uint32_t>(beam) + 31u) & ~31u;
+            for (uint32_t j0 = start; j0 < lim; j0 += 32) {
+                const uint32_t j = j0 + lane;
+                uint32_t e = 0;
+                const bool np = j < static_cast<uint32_t>(beam) && ((e = bidx[j]) & kMsb) == 0;
+                const uint32_t b = __ballot_sync(kFull, np);
+                const uint32_t i = __popc(b & lanemask_lt(lane)) + num;
+                if (np && i < theta) {
+                    s.pnode[i] = e & 0x7fffffffu;
+                    s.pdist[i] = bdist[j];
+                    bidx[j] = e | kMsb;
+                }
+                if (num + __popc(b) >= theta) {
+                    const uint32_t sel = __ballot_sync(kFull, np && i == theta - 1);
+                    last_pick = j0 + (__ffs(sel) - 1);
+                    num = theta;
+                    const uint32_t later = b & ~((sel << 1) - 1u);
+                    if ((later >> lane) & 1u) {
+                        const char* blk = reinterpret_cast<const char*>(rows + static_cast<uint64_t>(e & 0x7fffffffu) * rowf +
+                                                                        a.code_off);
+#pragma unroll
+                        for (int l = 0; l < 8; ++l) asm volatile("prefetch.global.L2 [%0];" ::"l"(blk + 128 * l));
+                    }
+                    break;
+                }
+                num += __popc(b);
+            }
+            __syncwarp();
+            if constexpr (mp) c.scan = num == theta ? last_pick + 1 : static_cast<uint32_t>(beam);
+            if (num) {
+                c.last_d = finite_lt_max(c.cur_d) ? c.cur_d : c.entry_d;
+                c.cur_d = s.pdist[num - 1];
+            }
+            if (a.trace && iter < a.trace_cap) {
+                const size_t base = static_cast<size_t>(qid) * a.trace_cap + iter;
+                if (lane < SEARCH_WIDTH)
+                    a.trace[base * SEARCH_WIDTH + lane] = lane < static_cast<int>(num) ? s.pnode[lane] : kMax;
+                if (lane == 0) a.trace_count[base] = static_cast<int32_t>(num);
+            }
+            if (lane == 0) {
+                ctl->stop = num == 0;
+                ctl->num = num;
+                ctl->th = c.theta;
+                ctl->rho = c.rho;
+                ctl->cutoff = cutoff;
+            }
+            c_exp += num;
+        }
+        pair_sync(bar);
+        if (ctl->stop) break;  // the same on both warps
+        const uint32_t num = ctl->num;
+        const int th = ctl->th;
+        const float rho = ctl->rho;
+        const float cutoff = ctl->cutoff;
+        const bool cut_ok = isfinite(cutoff) && cutoff < FLT_MAX;
+
+        if (!(th > 1)) {
+            // ---------------------------- single expander (src/adaptive_search.cuh:221-343), leader only
+            if (lead) {
+                const uint32_t work = static_cast<uint32_t>(deg) < cbs ? static_cast<uint32_t>(deg) : cbs;
+                const float* prow = rows + static_cast<uint64_t>(s.pnode[0]) * rowf;
+                const float pd = s.pdist[0];
+                ParentLane<W> p;
+                load_parent_pinned<W>(prow, a, static_cast<int>(work), vec, lane, p);
+                const bool in_work = static_cast<uint32_t>(lane) < work;
+                uint32_t child = p.child;
+                if (child != kMax && (child >= a.n || w_contains(s.hash, slots, child))) child = kMax;
+                float dist = child == kMax ? FLT_MAX : 0.0f;
+                const int keep = keep_for(work, th, rho, false, 0);
+                const uint32_t vcount = __popc(__ballot_sync(kFull, in_work && child != kMax));
+                int admit = static_cast<int>(work);
+                if (keep < static_cast<int>(vcount)) {
+                    if (child != kMax) {
+                        // theta = 1 variant: triple_x == FLT_MAX estimates 0.0 (include/utils.cuh:951-952)
+                        float est = 0.0f;
+                        if (p.tx != FLT_MAX) {
+                            const uint32_t raw = parent_raw<W>(p, prow, a, lane, s.planes, s.wrap, qsl.wrap_any);
+                            est = estimate(raw, p.tx, p.fdq, p.fvq, pd, qsl);
+                        }
+                        if (isfinite(est)) {
+                            dist = est;
+                        } else {
+                            dist = FLT_MAX;
+                            child = kMax;
+                        }
+                    }
+                    n_est += vcount;
+                    const uint32_t near =
+                        cut_ok ? __popc(__ballot_sync(kFull, in_work && child != kMax && isfinite(dist) && dist <= cutoff)) : 0u;
+                    const int eff = keep_for(work, th, rho, cut_ok, near);
+                    float kk = lane < static_cast<int>(cbs) ? dist : FLT_MAX;
+                    uint32_t vv = lane < static_cast<int>(cbs) ? child : kMax;
+                    sort32(kk, vv, lane);
+                    if (lane >= eff) {
+                        kk = FLT_MAX;
+                        vv = kMax;
+                    }
+                    dist = kk;
+                    child = vv;
+                    admit = eff;
+                }
+                const bool want = lane < admit && child != kMax && dist < FLT_MAX;
+                const uint32_t same = __match_any_sync(kFull, want ? child : kMax);
+                const bool first = want && (__ffs(same) - 1) == lane;
+                const bool ins = first && w_insert(s.hash, slots, child);
+                if (lane < static_cast<int>(cbs)) s.cidx[lane] = ins ? child : kMax;
+                const uint32_t ib = __ballot_sync(kFull, ins);
+                if (ins) {
+                    const uint32_t r = __popc(ib & lanemask_lt(lane));
+                    s.stage[r] = child;
+                    s.eslot[r] = lane;
+                    prefetch_row(rows + static_cast<uint64_t>(child) * rowf, dim);
+                }
+                __syncwarp();
+                const int ne = __popc(ib);
+                c_eval += ne;
+                if (lane == 0) ctl->ev_n = ne;
+            }
+        } else {
+            // ----------------------- speculative expanders (src/adaptive_search.cuh:344-444)
+            // this warp's parents t = role, role + 2, ...; lane l holds neighbour l
+            const uint32_t active = static_cast<uint32_t>(deg) < 32u ? static_cast<uint32_t>(deg) : 32u;
+            const int keep0 = keep_for(active, th, rho, false, 0);
+            const int cap = keep_cap(active, th, rho);
+            ParentLane<W> cur;
+            if (static_cast<uint32_t>(role) < num)
+                load_parent_pinned<W>(rows + static_cast<uint64_t>(s.pnode[role]) * rowf, a, deg, vec, lane, cur);
+#pragma unroll 1
+            for (int t = role; t < static_cast<int>(num); t += 2) {
+                const int tn = t + 2 < static_cast<int>(num) ? t + 2 : t;
+                ParentLane<W> nxt;
+                load_parent_pinned<W>(rows + static_cast<uint64_t>(s.pnode[tn]) * rowf, a, deg, vec, lane, nxt);
+                const uint32_t child = cur.child;
+                bool valid = child != kMax && child < a.n && !w_contains(s.hash, slots, child);
+                const uint32_t raw_valid = __popc(__ballot_sync(kFull, valid));
+                bool kl;
+                if (keep0 >= static_cast<int>(raw_valid)) {
+                    kl = valid;
+                } else {
+                    float est = FLT_MAX;
+                    if (valid) {
+                        // speculative variant: triple_x == FLT_MAX estimates FLT_MAX
+                        if (cur.tx != FLT_MAX) {
+                            uint32_t raw;
+                            if constexpr (W % 4 == 0) {
+                                raw = raw_sum_v<W>(cur.c, s.planes, s.wrap, qsl.wrap_any);
+                            } else {
+                                const float* prow = rows + static_cast<uint64_t>(s.pnode[t]) * rowf;
+                                raw = parent_raw<W>(cur, prow, a, lane, s.planes, s.wrap, qsl.wrap_any);
+                            }
+                            est = estimate(raw, cur.tx, cur.fdq, cur.fvq, s.pdist[t], qsl);
+                        }
+                        valid = isfinite(est);
+                    }
+                    n_est += raw_valid;
+                    const int near = __popc(__ballot_sync(kFull, valid && cut_ok && est <= cutoff));
+                    int eff = cut_ok ? (near < 1 ? 1 : (near > cap ? cap : near)) : cap;
+                    eff = eff < 1 ? 1 : (eff > static_cast<int>(active) ? static_cast<int>(active) : eff);
+                    kl = keep_smallest(est, valid, eff, lane);
+                }
+                const uint32_t kb = __ballot_sync(kFull, kl);
+                if (kl) {
+                    kp[t * 32 + __popc(kb & lanemask_lt(lane))] = child;
+                    prefetch_row(rows + static_cast<uint64_t>(child) * rowf, dim);
+                }
+                if (lane == 0) ctl->kc[t] = __popc(kb);
+                cur = nxt;
+            }
+            pair_sync(bar);
+            if (lead) {
+                // the kept children in (parent, rank) order, the first 32;
+                // a child kept by two parents goes to the first (include/utils.cuh:187-214)
+                uint32_t child = kMax;
+                uint32_t base = 0;
+                for (uint32_t t = 0; t < num; ++t) {
+                    const uint32_t k = ctl->kc[t];
+                    if (static_cast<uint32_t>(lane) >= base && static_cast<uint32_t>(lane) < base + k)
+                        child = kp[t * 32 + (lane - base)];
+                    base += k;
+                }
+                const uint32_t same = __match_any_sync(kFull, child);
+                const bool first = child != kMax && (__ffs(same) - 1) == lane;
+                const bool ins = first && w_insert(s.hash, slots, child);
+                const uint32_t ib = __ballot_sync(kFull, ins);
+                const uint32_t slot = __popc(ib & lanemask_lt(lane));
+                const uint32_t compact = __popc(ib);
+                const uint32_t ne = compact < pl.collect_cap ? compact : pl.collect_cap;
+                if (ins && slot < pl.collect_cap) s.cidx[slot] = child;
+                __syncwarp();
+                c_eval += ne;
+                if (lane == 0) ctl->ev_n = static_cast<int>(ne);
+            }
+        }
+        pair_sync(bar);
+        // exact distances, rounds split between the two warps
+        const int ev_n = ctl->ev_n;
+        if (th > 1) eval_nodes<W, G, IP>(rows, rowf, dim, qr, s.cidx, ev_n, s.cdist, nullptr, lane, role * G, 2 * G);
+        else eval_nodes<W, G, IP>(rows, rowf, dim, qr, s.stage, ev_n, s.cdist, s.eslot, lane, role * G, 2 * G);
+        pair_sync(bar);
+    }
+    if (!lead && lane == 0) ctl->nest_f = n_est;
+    pair_sync(bar);
+    if (!lead) return;
+    // final merge (src/adaptive_search.cuh:448-452)
+    if constexpr (mp) {
+        merge_path_warp(s, cbs, P, pl.mp_active, bnd, lane);
+    } else {
+        merge_bitonic<MERGE>(bidx, bdist, s.cidx, s.cdist, cbs, false, lane);
+    }
+    __syncwarp();
+    for (int i = lane; i < a.K; i += 32) {
+        const int sp = i < beam ? i : beam - 1;
+        a.out_ids[static_cast<size_t>(qid) * a.K + i] = bidx[sp] & 0x7fffffffu;
+        if (a.out_dists) a.out_dists[static_cast<size_t>(qid) * a.K + i] = bdist[sp];
+    }
+    if (lane == 0 && a.stats) {
+        fg_query_stats st;
+        st.iterations = c_iters;
+        st.expansions = c_exp;
+        st.evaluations = c_eval;
+        st.estimates = n_est + ctl->nest_f;
+        a.stats[qid] = st;
+    }
+    __syncwarp();
+}
+
+template <int W, int MERGE, bool IP, int MINB, int MODE>
 __global__ void __launch_bounds__(kWarpsPerCta * 32, MINB) search_warp_kernel(const SearchArgs a, const WPlan pl,
                                                                                   int vec_codes) {
-    constexpr bool kStaged = MINB == kCtasStaged;
+    constexpr bool kStaged = MODE == kModeStaged;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     // merge-path output segment boundaries s * itopk / active (launch constants)
     __shared__ uint16_t bnd[MERGE == 0 ? BLOCK_SIZE + 1 : 1];
@@ -1100,46 +1464,68 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, MINB) search_warp_kernel(co
         for (int sg = threadIdx.x; sg <= pl.mp_active; sg += blockDim.x)
             bnd[sg] = static_cast<uint16_t>((static_cast<uint32_t>(sg) * pl.padded) / static_cast<uint32_t>(pl.mp_active));
     }
-    __syncthreads();  // the only block barrier: the warps are independent from here on
+    __syncthreads();  // the only block-wide barrier: warps (or pairs of warps) are independent from here on
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    WSlice s;
-    slice_layout(pl.padded, pl.slots, 32 * W, MERGE == 0, &s, smem_raw + static_cast<size_t>(warp) * pl.slice,
-                 kStaged ? static_cast<size_t>(SEARCH_WIDTH) * pl.blk : 0);
-    for (;;) {
-        uint32_t qid = 0;
-        if (lane == 0) qid = atomicAdd(a.work_counter, 1u);
-        qid = __shfl_sync(kFull, qid, 0);
-        if (qid >= static_cast<uint32_t>(a.nq)) break;
-        search_query<W, MERGE, IP, kStaged>(a, pl, s, bnd, qid, vec_codes != 0, lane);
+    if constexpr (MODE == kModePair) {
+        const int pair = warp >> 1, role = warp & 1, bar = 1 + pair;
+        WSlice s;
+        slice_layout(pl.padded, pl.slots, 32 * W, MERGE == 0, &s, smem_raw + static_cast<size_t>(pair) * pl.slice,
+                     kPairExtraBytes);
+        PairCtl* ctl = reinterpret_cast<PairCtl*>(s.ring);
+        uint32_t* kp = reinterpret_cast<uint32_t*>(s.ring + kPairCtlBytes);
+        for (;;) {
+            if (role == 0 && lane == 0) ctl->qid = atomicAdd(a.work_counter, 1u);
+            pair_sync(bar);
+            const uint32_t qid = ctl->qid;
+            if (qid >= static_cast<uint32_t>(a.nq)) break;  // the same on both warps
+            search_query_pair<W, MERGE, IP>(a, pl, s, ctl, kp, bnd, qid, vec_codes != 0, lane, role, bar);
+        }
+    } else {
+        WSlice s;
+        slice_layout(pl.padded, pl.slots, 32 * W, MERGE == 0, &s, smem_raw + static_cast<size_t>(warp) * pl.slice,
+                     kStaged ? static_cast<size_t>(SEARCH_WIDTH) * pl.blk : 0);
+        for (;;) {
+            uint32_t qid = 0;
+            if (lane == 0) qid = atomicAdd(a.work_counter, 1u);
+            qid = __shfl_sync(kFull, qid, 0);
+            if (qid >= static_cast<uint32_t>(a.nq)) break;
+            search_query<W, MERGE, IP, kStaged>(a, pl, s, bnd, qid, vec_codes != 0, lane);
+        }
     }
 }
 
-template <int W, bool IP, int MINB>
+template <int W, bool IP, int MINB, int MODE>
 const void* pick_merge_w(int merge) {
     switch (merge) {
-        case 1: return reinterpret_cast<const void*>(search_warp_kernel<W, 1, IP, MINB>);
-        case 2: return reinterpret_cast<const void*>(search_warp_kernel<W, 2, IP, MINB>);
-        case 4: return reinterpret_cast<const void*>(search_warp_kernel<W, 4, IP, MINB>);
-        default: return reinterpret_cast<const void*>(search_warp_kernel<W, 0, IP, MINB>);
+        case 1: return reinterpret_cast<const void*>(search_warp_kernel<W, 1, IP, MINB, MODE>);
+        case 2: return reinterpret_cast<const void*>(search_warp_kernel<W, 2, IP, MINB, MODE>);
+        case 4: return reinterpret_cast<const void*>(search_warp_kernel<W, 4, IP, MINB, MODE>);
+        default: return reinterpret_cast<const void*>(search_warp_kernel<W, 0, IP, MINB, MODE>);
     }
 }
 
-template <bool IP, int MINB>
+template <bool IP, int MINB, int MODE>
 const void* pick_w(int W, int merge) {
     switch (W) {
-        case 1: return pick_merge_w<1, IP, MINB>(merge);
-        case 2: return pick_merge_w<2, IP, MINB>(merge);
-        case 4: return pick_merge_w<4, IP, MINB>(merge);
-        default: return pick_merge_w<8, IP, MINB>(merge);
+        case 1: return pick_merge_w<1, IP, MINB, MODE>(merge);
+        case 2: return pick_merge_w<2, IP, MINB, MODE>(merge);
+        case 4: return pick_merge_w<4, IP, MINB, MODE>(merge);
+        default: return pick_merge_w<8, IP, MINB, MODE>(merge);
     }
 }
 
-// kernel for W = padded dim / 32, the beam merge, the metric and the register
-// budget (kCtasStaged: the staged variant)
-const void* warp_kernel_for(int W, int merge, bool ip, int minb) {
-    if (minb == kCtasSmall) return ip ? pick_w<true, kCtasSmall>(W, merge) : pick_w<false, kCtasSmall>(W, merge);
-    if (minb == kCtasStaged) return ip ? pick_w<true, kCtasStaged>(W, merge) : pick_w<false, kCtasStaged>(W, merge);
-    return ip ? pick_w<true, kCtasLarge>(W, merge) : pick_w<false, kCtasLarge>(W, merge);
+template <int MINB, int MODE>
+const void* pick_ip(int W, int merge, bool ip) {
+    return ip ? pick_w<true, MINB, MODE>(W, merge) : pick_w<false, MINB, MODE>(W, merge);
+}
+
+// kernel for W = padded dim / 32, the beam merge, the metric, the register
+// budget and the mode (one warp per query; staged; a pair of warps per query)
+const void* warp_kernel_for(int W, int merge, bool ip, int minb, int mode) {
+    if (mode == kModePair) return pick_ip<kCtasPair, kModePair>(W, merge, ip);
+    if (mode == kModeStaged) return pick_ip<kCtasStaged, kModeStaged>(W, merge, ip);
+    if (minb == kCtasSmall) return pick_ip<kCtasSmall, kModeWarp>(W, merge, ip);
+    return pick_ip<kCtasLarge, kModeWarp>(W, merge, ip);
 }
 
 }  // namespace
@@ -1156,7 +1542,9 @@ bool warp_staged_supported(const SearchArgs& a, const SearchPlan& p) {
     return p.vec_codes && (parent_block_bytes(a) % 16) == 0;
 }
 
-int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, size_t errlen, bool staged) {
+// mode: kModeWarp (one warp per query), kModeStaged (falls back to kModeWarp
+// where the blocks are not 16-byte aligned) or kModePair (two warps per query).
+int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, size_t errlen, int mode) {
     const int D = a.padded_dim;
     uint32_t req = p->padded + p->cbs * SMALL_HASH_RESET_INTERVAL;
     uint32_t slots = req + (req + 11) / 12;  // ~93 % at the bound (two-choice buckets)
@@ -1166,10 +1554,14 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
     slots = (slots + 31) & ~31u;
     p->kernel = 1;
     p->slots = slots;
-    staged = staged && warp_staged_supported(a, *p);
-    p->blk = staged ? parent_block_bytes(a) : 0;
-    p->slice_bytes = slice_layout(p->padded, slots, D, p->merge_n2 == 0, nullptr, nullptr,
-                                  static_cast<size_t>(SEARCH_WIDTH) * p->blk);
+    if (mode == kModeStaged && !warp_staged_supported(a, *p)) mode = kModeWarp;
+    p->warp_mode = mode;
+    p->blk = mode == kModeStaged ? parent_block_bytes(a) : 0;
+    const size_t extra = mode == kModeStaged ? static_cast<size_t>(SEARCH_WIDTH) * p->blk
+                         : mode == kModePair ? kPairExtraBytes : 0;
+    // bytes per query (per warp, or per pair of warps in the pair mode)
+    p->slice_bytes = slice_layout(p->padded, slots, D, p->merge_n2 == 0, nullptr, nullptr, extra);
+    const int warps_per_query = mode == kModePair ? 2 : 1;
     int sms = 0, max_smem = 0;
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
@@ -1186,12 +1578,17 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
     // go to the larger CTA
     const void* best = nullptr;
     int best_q = 0;
-    const int budgets[2] = {staged ? kCtasStaged : kCtasSmall, staged ? kCtasStaged : kCtasLarge};
-    for (int bi = 0; bi < (staged ? 1 : 2); ++bi) {
+    int budgets[2] = {kCtasSmall, kCtasLarge};
+    int nbudgets = 2;
+    if (mode == kModeStaged) budgets[0] = kCtasStaged, nbudgets = 1;
+    if (mode == kModePair) budgets[0] = kCtasPair, nbudgets = 1;
+    for (int bi = 0; bi < nbudgets; ++bi) {
         const int minb = budgets[bi];
-        const void* fn = warp_kernel_for(D / 32, p->merge_n2, a.use_ip != 0, minb);
+        const void* fn = warp_kernel_for(D / 32, p->merge_n2, a.use_ip != 0, minb, mode);
         for (int wpc : {kWarpsPerCta, 2, 1}) {
-            const size_t smem = p->slice_bytes * static_cast<size_t>(wpc);
+            if (wpc % warps_per_query) continue;
+            const int qpc = wpc / warps_per_query;
+            const size_t smem = p->slice_bytes * static_cast<size_t>(qpc);
             if (smem > static_cast<size_t>(max_smem)) continue;
             e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
             if (e == cudaSuccess)
@@ -1202,8 +1599,8 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
                 snprintf(err, errlen, "occupancy query failed: %s", cudaGetErrorString(e));
                 return FG_ERR_CUDA;
             }
-            if (per_sm * wpc > best_q) {
-                best_q = per_sm * wpc;
+            if (per_sm * qpc > best_q) {
+                best_q = per_sm * qpc;
                 best = fn;
                 p->min_ctas = minb;
                 p->threads = wpc * 32;
@@ -1221,11 +1618,12 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
         snprintf(err, errlen, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         return FG_ERR_CUDA;
     }
-    const int wpc = p->threads / 32;
+    const int qpc = p->threads / 32 / warps_per_query;
     const int resident = p->blocks_per_sm * sms;
-    const int need = (a.nq + wpc - 1) / wpc;
+    const int need = (a.nq + qpc - 1) / qpc;
     p->grid = need < resident ? need : resident;
     if (p->grid < 1) p->grid = 1;
+    p->resident_queries = resident * qpc;
     return FG_OK;
 }
 
@@ -1242,7 +1640,7 @@ cudaError_t launch_search_warp(const SearchArgs& a, const SearchPlan& p, cudaStr
     pl.blk = p.blk;
     cudaError_t e = cudaMemsetAsync(a.work_counter, 0, sizeof(uint32_t), stream);
     if (e != cudaSuccess) return e;
-    const void* fn = warp_kernel_for(a.padded_dim / 32, p.merge_n2, a.use_ip != 0, p.min_ctas);
+    const void* fn = warp_kernel_for(a.padded_dim / 32, p.merge_n2, a.use_ip != 0, p.min_ctas, p.warp_mode);
     SearchArgs args = a;
     int vec = p.vec_codes;
     void* params[] = {&args, &pl, &vec};

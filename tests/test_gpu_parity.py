@@ -54,11 +54,12 @@ def _run_gpu(qg, queries, K, beam, trace_cap=0):
     return out
 
 
-@pytest.fixture(params=["warp", "staged", "cta"])
+@pytest.fixture(params=["warp", "staged", "pair", "cta"])
 def kernel(request, monkeypatch):
     """Every search kernel: the warp kernel, its staged variant (parent blocks
-    copied to shared memory with cp.async) and the CTA kernel (the planner
-    picks by batch size; FG_KERNEL forces one)."""
+    copied to shared memory with cp.async), its pair mode (two warps per
+    query) and the CTA kernel (the planner picks by batch size; FG_KERNEL
+    forces one)."""
     monkeypatch.setenv("FG_KERNEL", request.param)
     return request.param
 

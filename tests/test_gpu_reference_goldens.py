@@ -25,7 +25,7 @@ pytestmark = pytest.mark.gpu
 SETS = ["c1_100k", "t_20k", "t_8k16", "t_2k", "t_2k_ip"]
 
 
-@pytest.fixture(params=["warp", "staged", "cta"])
+@pytest.fixture(params=["warp", "staged", "pair", "cta"])
 def kernel(request, monkeypatch):
     monkeypatch.setenv("FG_KERNEL", request.param)
     return request.param
