@@ -731,12 +731,14 @@ int variant_from_env() {
     return (x >= 0 && x < kNumVariants) ? x : kDefaultVariant;
 }
 
-// Kernel choice where both apply (padded dim <= 256; they return identical
-// results): the warp kernel for batches of more than 4 queries per SM, where
-// its 20 resident queries per SM pay; below that the CTA kernel's 8 warps per
-// query finish sooner.  FG_KERNEL=warp, =staged (the warp kernel's staged
-// variant) or =cta forces one.
-enum class Choice { kCta, kWarp, kStaged, kPair };
+// Kernel choice where all apply (padded dim <= 256; they return identical
+// results), by queries per SM, from batch sweeps on a B200: up to 4 the CTA
+// kernel (8 warps per query: the shortest time per query), up to what the
+// pair mode holds resident (10) the warp kernel's pair mode (2 warps per
+// query), above that one warp per query (20 resident queries per SM at beam
+// <= 640 and D = 128).  FG_KERNEL=cta, =pair, =warp or =staged (the warp
+// kernel's staged variant) forces one.
+enum class Choice { kCta, kWarp, kStaged, kPair, kAuto };
 
 Choice kernel_choice(int nq, int device) {
     const char* v = getenv("FG_KERNEL");
@@ -746,7 +748,7 @@ Choice kernel_choice(int nq, int device) {
     if (v && v[0] == 'p') return Choice::kPair;
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) sms = 148;
-    return nq > 4 * sms ? Choice::kWarp : Choice::kCta;
+    return nq > 4 * sms ? Choice::kAuto : Choice::kCta;
 }
 
 int merge_width(uint32_t itopk) {
@@ -822,6 +824,12 @@ int plan_search(const SearchArgs& a, SearchPlan* p, int device, char* err, size_
     p->vec_codes = ((base % 16) == 0 && ((a.row * 4) % 16) == 0 && ((a.code_off * 4) % 16) == 0) ? 1 : 0;
     if (warp_kernel_supports(a.padded_dim)) {
         const Choice c = kernel_choice(a.nq, device);
+        if (c == Choice::kAuto) {
+            // the pair mode while the whole batch is resident at once, else one warp per query
+            const int rc = plan_search_warp(a, p, device, err, errlen, 2);
+            if (rc != FG_OK || a.nq <= p->resident_queries) return rc;
+            return plan_search_warp(a, p, device, err, errlen, 0);
+        }
         if (c != Choice::kCta)
             return plan_search_warp(a, p, device, err, errlen, c == Choice::kStaged ? 1 : c == Choice::kPair ? 2 : 0);
     }

@@ -56,16 +56,19 @@ constexpr int kCtasSmall = 5;
 // The staged variant (3 CTAs per SM, 168 registers): every parent block of a
 // speculative iteration is copied into a shared-memory ring with cp.async at
 // once, instead of one block ahead in registers, and exact distances run 16
-// rows per round.  It shortens each query's dependent chain of loads and is
-// the planner's choice for batches that leave most warp slots idle.
+// rows per round.  On a B200 it was no faster than the register pipeline at
+// any batch size (a lone query's time is set by its chain of instructions,
+// not by the parent loads) and slower at full batches (12 instead of 20
+// resident queries per SM), so the planner never picks it; FG_KERNEL=staged
+// selects it.
 constexpr int kCtasStaged = 3;
 // Kernel modes: one warp per query, the staged variant of it, or a pair of
 // warps per query (the pair mode, for batches that fill few warp slots).
 constexpr int kModeWarp = 0;
 constexpr int kModeStaged = 1;
 constexpr int kModePair = 2;
-// The pair mode's register budget: 4 CTAs of 4 warps (2 queries) per SM.
-constexpr int kCtasPair = 4;
+// The pair mode's register budget: 5 CTAs of 4 warps (10 queries) per SM.
+constexpr int kCtasPair = 5;
 
 struct WPlan {
     uint32_t padded, cbs, collect_cap;
