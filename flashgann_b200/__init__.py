@@ -121,6 +121,61 @@ class QuantizationGraph:
         self.gpu_search_adaptive(q.shape[0], q, K, out, beam)
         return out
 
+    def search_async(self, slot: int, nq: int, queries: np.ndarray, K: int, result_idx: np.ndarray, beam: int,
+                     stream) -> None:
+        """Enqueue one host-buffer batch on `stream` (fg_search_async): upload,
+        search and download of the ids into result_idx, without waiting.
+        `slot` (0 .. FG_ASYNC_SLOTS-1) picks the index's device buffers; keep
+        `queries` and `result_idx` alive (and pinned, for overlap) until the
+        stream has been synchronised."""
+        if result_idx.dtype != np.uint32 or not result_idx.flags.c_contiguous or result_idx.size < nq * K:
+            raise FlashGANNError(FG_ERR_ARG, "result_idx must be a contiguous uint32 array of nq*K")
+        if queries.dtype != np.float32 or not queries.flags.c_contiguous or queries.size < nq * self.dim:
+            raise FlashGANNError(FG_ERR_ARG, "queries must be a contiguous float32 array of nq*dim")
+        s = getattr(stream, "cuda_stream", stream) or 0
+        _check(lib().fg_search_async(self._h, slot, nq, queries.ctypes.data_as(ctypes.c_void_p), K,
+                                     result_idx.ctypes.data_as(ctypes.c_void_p), beam, ctypes.c_void_p(s)),
+               "fg_search_async")
+
+    def search_stream(self, batches, K: int, beam: int, depth: int = 2):
+        """Pipelined search of an iterable of query batches (float32 [m, dim]
+        each): yields the ids (uint32 [m, K]) of every batch in order.  Up to
+        `depth` batches are in flight, each with its own slot, stream and
+        pinned staging buffers, so one batch's upload and download overlap
+        another's search."""
+        import torch
+        if not 1 <= depth <= _capi.FG_ASYNC_SLOTS:
+            raise FlashGANNError(FG_ERR_ARG, f"depth must be in [1, {_capi.FG_ASYNC_SLOTS}]")
+        streams = [torch.cuda.Stream(device=self.device) for _ in range(depth)]
+        staged = [None] * depth  # (pinned queries, pinned ids, m) per slot
+        pending = []  # slots in submission order
+
+        def take(slot):
+            streams[slot].synchronize()
+            _, hres, m = staged[slot]
+            return hres[:m * K].reshape(m, K).copy()
+
+        n = 0
+        for b in batches:
+            q = np.ascontiguousarray(b, dtype=np.float32).reshape(-1, self.dim)
+            m = q.shape[0]
+            slot = n % depth
+            if len(pending) == depth:
+                yield take(pending.pop(0))
+            cur = staged[slot]
+            if cur is None or cur[0].size < q.size or cur[1].size < m * K:
+                hq = torch.empty(max(q.size, 1), dtype=torch.float32).pin_memory().numpy()
+                hr = torch.empty(max(m * K, 1), dtype=torch.int32).pin_memory().numpy().view(np.uint32)
+                cur = (hq, hr, m)
+            hq, hr, _ = cur
+            hq[:q.size] = q.reshape(-1)
+            staged[slot] = (hq, hr, m)
+            self.search_async(slot, m, hq, K, hr, beam, streams[slot])
+            pending.append(slot)
+            n += 1
+        while pending:
+            yield take(pending.pop(0))
+
     def search_device(self, d_queries, K: int, beam: int, d_out=None, d_dists=None, stream=None, d_stats=None,
                       d_trace=None, d_trace_count=None, trace_cap: int = 0):
         """Asynchronous search on device buffers (torch CUDA tensors or raw

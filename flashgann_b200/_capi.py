@@ -20,6 +20,7 @@ FG_ERR_UNSUPPORTED = 6
 FG_ERR_NO_DEVICE = 7
 FG_METRIC_L2 = 0
 FG_METRIC_IP = 1
+FG_ASYNC_SLOTS = 4
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libflashgann.so")
 
@@ -59,6 +60,7 @@ SIGNATURES = [
     ("fg_index_set_metric", ctypes.c_int, [_vp, _i32]),
     ("fg_search", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _i32, ctypes.POINTER(_f64)]),
     ("fg_search_noalloc", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _i32, ctypes.POINTER(_f64)]),
+    ("fg_search_async", ctypes.c_int, [_vp, _i32, _i32, _vp, _i32, _vp, _i32, _vp]),
     ("fg_search_multi", ctypes.c_int, [ctypes.POINTER(_vp), _i32, _i32, _vp, _i32, _vp, _vp, _i32, ctypes.POINTER(_f64)]),
     ("fg_search_device", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp]),
     ("fg_search_device_ex", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _i32]),

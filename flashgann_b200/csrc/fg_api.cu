@@ -35,6 +35,14 @@ struct fg_index {
     size_t cap_dists = 0;
     uint32_t* d_counter = nullptr;  // persistent-CTA work counter
     cudaStream_t stream = nullptr;
+    // fg_search_async: per-slot device buffers and work counter, grown on demand
+    struct AsyncSlot {
+        float* d_queries = nullptr;
+        size_t cap_queries = 0;
+        uint32_t* d_results = nullptr;
+        size_t cap_results = 0;
+        uint32_t* d_counter = nullptr;
+    } slots[FG_ASYNC_SLOTS];
 };
 
 namespace {
@@ -158,6 +166,11 @@ void destroy(fg_index* x) {
     if (x->d_results) cudaFree(x->d_results);
     if (x->d_dists) cudaFree(x->d_dists);
     if (x->d_counter) cudaFree(x->d_counter);
+    for (auto& sl : x->slots) {
+        if (sl.d_queries) cudaFree(sl.d_queries);
+        if (sl.d_results) cudaFree(sl.d_results);
+        if (sl.d_counter) cudaFree(sl.d_counter);
+    }
     if (x->stream) cudaStreamDestroy(x->stream);
     delete x;
 }
@@ -460,6 +473,43 @@ int fg_search(fg_index* x, int32_t nq, const float* queries, int32_t K, uint32_t
     if ((e = cudaMemcpyAsync(result_idx, x->d_results, rn * sizeof(uint32_t), cudaMemcpyDeviceToHost, x->stream)) != cudaSuccess)
         return cuda_fail(e, "cudaMemcpyAsync(results)");
     if ((e = cudaStreamSynchronize(x->stream)) != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    return FG_OK;
+}
+
+int fg_search_async(fg_index* x, int32_t slot, int32_t nq, const float* queries, int32_t K, uint32_t* result_idx,
+                    int32_t beam, void* stream) {
+    g_err.clear();
+    if (!x) return fail(FG_ERR_ARG, "null index");
+    if (slot < 0 || slot >= FG_ASYNC_SLOTS) return fail(FG_ERR_ARG, "slot %d outside [0, %d)", slot, FG_ASYNC_SLOTS);
+    if (nq < 0) return fail(FG_ERR_ARG, "nq must be >= 0 (got %d)", nq);
+    if (nq > 0 && (!queries || !result_idx)) return fail(FG_ERR_ARG, "null query or result buffer");
+    DeviceGuard g(x->device);
+    if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
+    fg::SearchArgs a = base_args(x);
+    a.nq = nq;
+    a.K = K;
+    a.beam = beam;
+    fg::SearchPlan plan;
+    char err[256];
+    int rc = fg::plan_search(a, &plan, x->device, err, sizeof(err));
+    if (rc) return fail(rc, "%s", err);
+    if (nq == 0) return FG_OK;
+    fg_index::AsyncSlot& sl = x->slots[slot];
+    const size_t qn = static_cast<size_t>(nq) * x->dim, rn = static_cast<size_t>(nq) * K;
+    if ((rc = grow(&sl.d_queries, &sl.cap_queries, qn, "queries")) != FG_OK) return rc;
+    if ((rc = grow(&sl.d_results, &sl.cap_results, rn, "results")) != FG_OK) return rc;
+    cudaError_t e;
+    if (!sl.d_counter && (e = cudaMalloc(&sl.d_counter, 256)) != cudaSuccess)
+        return fail(FG_ERR_OOM, "cudaMalloc(counter): %s", cudaGetErrorString(e));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    a.queries = sl.d_queries;
+    a.out_ids = sl.d_results;
+    a.work_counter = sl.d_counter;
+    if ((e = cudaMemcpyAsync(sl.d_queries, queries, qn * sizeof(float), cudaMemcpyHostToDevice, st)) != cudaSuccess)
+        return cuda_fail(e, "cudaMemcpyAsync(queries)");
+    if ((e = fg::launch_search(a, plan, st)) != cudaSuccess) return cuda_fail(e, "search launch");
+    if ((e = cudaMemcpyAsync(result_idx, sl.d_results, rn * sizeof(uint32_t), cudaMemcpyDeviceToHost, st)) != cudaSuccess)
+        return cuda_fail(e, "cudaMemcpyAsync(results)");
     return FG_OK;
 }
 

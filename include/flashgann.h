@@ -116,6 +116,24 @@ int fg_search(fg_index* index, int32_t nq, const float* queries, int32_t K, uint
 int fg_search_multi(fg_index* const* indexes, int32_t count, int32_t nq, const float* queries, int32_t K,
                     uint32_t* result_idx, float* result_dist, int32_t beam, double* elapsed_s);
 
+/* Number of buffer slots of fg_search_async per index. */
+#define FG_ASYNC_SLOTS 4
+
+/* Streamed variant of fg_search for pipelines of query batches (the
+ * reference re-uploads its index and synchronises on every call,
+ * gpu_search_adaptive.cu:65-113): enqueues on `stream` the upload of
+ * queries[nq*dim], the search and the download of the ids into
+ * result_idx[nq*K], and returns without waiting.  `slot` (0 ..
+ * FG_ASYNC_SLOTS-1) names the index's device buffers the batch uses, so
+ * batches in different slots may be in flight at once -- one slot per stream
+ * lets batch i+1's upload overlap batch i's search.  Host buffers should be
+ * pinned (cudaHostAlloc) for the copies to run asynchronously.  The caller
+ * synchronises the stream before reading result_idx and before reusing the
+ * slot or the host buffers.  The first use of a slot, or a larger batch than
+ * it has held, allocates its buffers. */
+int fg_search_async(fg_index* index, int32_t slot, int32_t nq, const float* queries, int32_t K, uint32_t* result_idx,
+                    int32_t beam, void* stream);
+
 /* Size of the fixed device scratch used by fg_search_noalloc (8 MiB). */
 #define FG_NOALLOC_SCRATCH_BYTES 8388608
 
