@@ -11,6 +11,7 @@
 #include <fstream>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include <cuda_runtime.h>
@@ -43,6 +44,9 @@ struct fg_index {
         size_t cap_results = 0;
         uint32_t* d_counter = nullptr;
     } slots[FG_ASYNC_SLOTS];
+    // work counters of fg_search_device, one per stream, so that searches on
+    // different streams may overlap on the device
+    std::vector<std::pair<cudaStream_t, uint32_t*>> stream_counters;
 };
 
 namespace {
@@ -171,6 +175,7 @@ void destroy(fg_index* x) {
         if (sl.d_results) cudaFree(sl.d_results);
         if (sl.d_counter) cudaFree(sl.d_counter);
     }
+    for (auto& sc : x->stream_counters) cudaFree(sc.second);
     if (x->stream) cudaStreamDestroy(x->stream);
     delete x;
 }
@@ -196,6 +201,26 @@ int grow(T** buf, size_t* cap, size_t n, const char* what) {
     cudaError_t e = cudaMalloc(buf, n * sizeof(T));
     if (e != cudaSuccess) return fail(FG_ERR_OOM, "cudaMalloc(%s): %s", what, cudaGetErrorString(e));
     *cap = n;
+    return FG_OK;
+}
+
+// The work counter fg_search_device uses on `stream` (allocated on the
+// stream's first search): launches on one stream run in order and share it,
+// launches on different streams get their own.
+constexpr size_t kMaxStreamCounters = 64;
+int stream_counter(fg_index* x, cudaStream_t stream, uint32_t** out) {
+    for (auto& sc : x->stream_counters)
+        if (sc.first == stream) {
+            *out = sc.second;
+            return FG_OK;
+        }
+    if (x->stream_counters.size() >= kMaxStreamCounters)
+        return fail(FG_ERR_UNSUPPORTED, "more than %zu streams searched one index", kMaxStreamCounters);
+    uint32_t* c = nullptr;
+    const cudaError_t e = cudaMalloc(&c, 256);
+    if (e != cudaSuccess) return fail(FG_ERR_OOM, "cudaMalloc(counter): %s", cudaGetErrorString(e));
+    x->stream_counters.emplace_back(stream, c);
+    *out = c;
     return FG_OK;
 }
 
@@ -415,6 +440,7 @@ int fg_search_device_ex(fg_index* x, int32_t nq, const float* d_queries, int32_t
     int rc = fg::plan_search(a, &plan, x->device, err, sizeof(err));
     if (rc) return fail(rc, "%s", err);
     if (nq == 0) return FG_OK;
+    if ((rc = stream_counter(x, static_cast<cudaStream_t>(stream), &a.work_counter)) != FG_OK) return rc;
     cudaError_t e = fg::launch_search(a, plan, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "search launch");
     return FG_OK;

@@ -1108,7 +1108,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
 // own, so the leader's compaction sees them in (parent, rank) order exactly
 // as the one-warp search does, and every visited-set lookup of an iteration
 // still precedes its inserts.  The two warps meet at a named barrier (64
-// threads, id 1 + the pair's index in the CTA) at points both reach on every
+// threads, one per pair of the CTA) at points both reach on every
 // path: after set-up, after the pick, after the parents, after the
 // compaction, after the distances, and at the end of the query.  Results are
 // the one-warp search's, bit for bit.
@@ -1129,7 +1129,13 @@ struct PairCtl {
 constexpr size_t kPairCtlBytes = (sizeof(PairCtl) + 15) & ~static_cast<size_t>(15);
 constexpr size_t kPairExtraBytes = kPairCtlBytes + static_cast<size_t>(SEARCH_WIDTH) * 32 * 4;
 
-__device__ __forceinline__ void pair_sync(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+// Barrier of the pair with index `pair` in its CTA (ids 1 and 2; 0 is
+// __syncthreads).  The ids are immediates: a barrier id in a register makes
+// ptxas reserve all 16 barriers of the CTA, which caps the CTAs per SM.
+__device__ __forceinline__ void pair_sync(int pair) {
+    if (pair == 0) asm volatile("bar.sync 1, 64;" ::: "memory");
+    else asm volatile("bar.sync 2, 64;" ::: "memory");
+}
 
 template <int W, int MERGE, bool IP>
 __device__ __forceinline__ void search_query_pair(const SearchArgs& a, const WPlan& pl, const WSlice& s, PairCtl* ctl,
@@ -1470,7 +1476,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, MINB) search_warp_kernel(co
     __syncthreads();  // the only block-wide barrier: warps (or pairs of warps) are independent from here on
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if constexpr (MODE == kModePair) {
-        const int pair = warp >> 1, role = warp & 1, bar = 1 + pair;
+        const int pair = warp >> 1, role = warp & 1, bar = pair;
         WSlice s;
         slice_layout(pl.padded, pl.slots, 32 * W, MERGE == 0, &s, smem_raw + static_cast<size_t>(pair) * pl.slice,
                      kPairExtraBytes);

@@ -161,7 +161,9 @@ int fg_search_noalloc(fg_index* index, int32_t nq, const float* queries, int32_t
 
 /* Device-resident variant: d_queries / d_result_idx / d_result_dist (optional)
  * are device pointers on the index's device; the call is asynchronous on
- * `stream` (a cudaStream_t, NULL = default stream). */
+ * `stream` (a cudaStream_t, NULL = default stream).  Searches on different
+ * streams may run at the same time (each stream gets its own work counter,
+ * allocated on its first search; at most 64 streams per index). */
 int fg_search_device(fg_index* index, int32_t nq, const float* d_queries, int32_t K, uint32_t* d_result_idx,
                      float* d_result_dist, int32_t beam, void* stream);
 
