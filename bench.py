@@ -409,18 +409,45 @@ def run_sharded(args, ws, rank, local):
     from flashgann_b200 import distributed as fgd
     torch.cuda.set_device(local)
     dev = f"cuda:{local}"
-    if rank == 0:
-        builder.materialize(args.config, device=dev, verbose=True)
-    _barrier(ws)
-    sh = builder.materialize_shard(args.config, rank, ws, device=dev, verbose=(rank == 0))
+    spec0 = builder.SPECS[args.config]
+    build_s = None
+    if spec0.block:
+        # a blocked spec: every rank draws and builds its own
+        # shard on its own GPU; the global ground truth is the merge of every
+        # shard's exact lists
+        import torch.distributed as dist
+        t0 = time.perf_counter()
+        sh = builder.materialize_shard_device(args.config, rank, ws, device=dev, verbose=(rank == 0))
+        qg = fg.QuantizationGraph.from_device(sh.rows, torch.from_numpy(sh.signs).to(dev), sh.entry, spec0.dim,
+                                              spec0.degree)
+        sh.rows = None
+        torch.cuda.empty_cache()
+        gi = torch.from_numpy(sh.gt_ids).to(dev)
+        gd = torch.from_numpy(sh.gt_d).to(dev)
+        if ws > 1:
+            all_i = [torch.empty_like(gi) for _ in range(ws)]
+            all_d = [torch.empty_like(gd) for _ in range(ws)]
+            dist.all_gather(all_i, gi)
+            dist.all_gather(all_d, gd)
+        else:
+            all_i, all_d = [gi], [gd]
+        gt = builder.merge_shard_ground_truth(np.stack([t.cpu().numpy() for t in all_i]),
+                                              np.stack([t.cpu().numpy() for t in all_d]), spec0.gt_k)
+        build_s = _max_over_ranks(time.perf_counter() - t0, ws)
+        queries = sh.queries
+    else:
+        if rank == 0:
+            builder.materialize(args.config, device=dev, verbose=True)
+        _barrier(ws)
+        sh = builder.materialize_shard(args.config, rank, ws, device=dev, verbose=(rank == 0))
+        qg = fg.QuantizationGraph(sh.n, spec0.dim, spec0.degree, sh.codebook_path, device=local)
+        queries, gt = sh.queries, sh.gt
     _barrier(ws)
     spec = sh.spec
     K = spec.K
-    queries, gt = sh.queries, sh.gt
     if args.queries:
         queries, gt = queries[:args.queries], gt[:args.queries]
     nq = len(queries)
-    qg = fg.QuantizationGraph(sh.n, spec.dim, spec.degree, sh.codebook_path, device=local)
     dq = torch.from_numpy(queries).to(dev)
     dout = torch.empty((nq, K), dtype=torch.int32, device=dev)
     dd = torch.empty((nq, K), dtype=torch.float32, device=dev)
@@ -459,6 +486,15 @@ def run_sharded(args, ws, rank, local):
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / args.steps
     ms_max = _max_over_ranks(ms, ws)
+    # the search alone (no all-gather, no merge), for the collective's share of a step
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        qg.search_device(dq, K, beam, d_out=dout, d_dists=dd, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    search_ms = _max_over_ranks(e0.elapsed_time(e1) / args.steps, ws)
+    _barrier(ws)
     # end to end: pinned host queries in, merged ids out, every step
     hq = torch.from_numpy(queries).pin_memory()
     hres = torch.empty((nq, K), dtype=torch.int32).pin_memory()
@@ -477,9 +513,14 @@ def run_sharded(args, ws, rank, local):
         "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": _data_name(spec),
         "config": {"workload": f"{spec.name} in {ws} shards", "n": spec.n, "shard_nodes": sh.n, "dim": spec.dim,
-                   "degree": spec.degree, "K": K, "queries": nq, "beam": beam, "recall_at_k": recall,
-                   "recall_table": table,
-                   "parallelism": f"index sharded x{ws} (per-shard graphs), all-gather of per-shard top-{K} + device merge"},
+                   "degree": spec.degree, "K": K, "queries_total": nq, "beam": beam,
+                   "parallelism": f"index sharded x{ws} (per-shard graphs), all-gather of per-shard top-{K} + "
+                                  "merge kernel (fg_shard_merge_device)",
+                   "l2": "inputs larger than L2 (shard codebook %.2f GB > 126 MB)" % (sh.n * sh.layout.row * 4 / 1e9)},
+        "recall": {"at_beam": recall, "curve": table},
+        "shard_build_s": build_s,
+        "step_breakdown_ms": {"search": search_ms, "all_gather_and_merge": ms_max - search_ms,
+                              "all_gather_bytes_per_rank": nq * K * 8},
         "e2e": {"value": nq / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": nq * spec.dim * 4,
                 "d2h_bytes_per_step": nq * K * 4},
         "gpu_launches": 2 * args.steps,

@@ -70,6 +70,23 @@ class QuantizationGraph:
         self._fill_layout()
         return self
 
+    @classmethod
+    def from_device(cls, rows, signs, entry_point: int, dim: int, degree: int, metric: int = METRIC_L2
+                    ) -> "QuantizationGraph":
+        """An index from a codebook already on a GPU (fg_index_create_device):
+        rows float32 [n, row_offset] and signs float32 [padded_dim], CUDA
+        tensors on the device the index will live on (copied there; the
+        tensors may be freed afterwards)."""
+        self = cls.__new__(cls)
+        self._h = ctypes.c_void_p()
+        rows = rows.contiguous()
+        signs = signs.contiguous()
+        _check(lib().fg_index_create_device(_capi.device_ptr(rows), _capi.device_ptr(signs), entry_point & 0xFFFFFFFF,
+                                            rows.shape[0], dim, degree, metric, rows.device.index or 0,
+                                            ctypes.byref(self._h)), "fg_index_create_device")
+        self._fill_layout()
+        return self
+
     def _fill_layout(self) -> None:
         L = _capi.Layout()
         _check(lib().fg_index_layout(self._h, ctypes.byref(L)), "fg_index_layout")

@@ -55,6 +55,7 @@ SIGNATURES = [
     ("fg_last_error", ctypes.c_char_p, []),
     ("fg_index_load", ctypes.c_int, [_cs, _u64, _u64, _i32, _i32, _i32, ctypes.POINTER(_vp)]),
     ("fg_index_create", ctypes.c_int, [_vp, _vp, _u32, _u64, _u64, _i32, _i32, _i32, ctypes.POINTER(_vp)]),
+    ("fg_index_create_device", ctypes.c_int, [_vp, _vp, _u32, _u64, _u64, _i32, _i32, _i32, ctypes.POINTER(_vp)]),
     ("fg_index_free", ctypes.c_int, [_vp]),
     ("fg_index_layout", ctypes.c_int, [_vp, ctypes.POINTER(Layout)]),
     ("fg_index_set_metric", ctypes.c_int, [_vp, _i32]),

@@ -101,6 +101,7 @@ class DatasetSpec:
     knn_k: int = 64
     gt_k: int = 100
     knn: str = "exact"         # graph candidates: exact | exact_tf32 | partitioned (see build_graph)
+    block: int = 0             # > 0: the base is drawn in blocks of this many rows, each from a stream of its own
 
 
 SPECS = {
@@ -124,10 +125,20 @@ SPECS = {
     "c4_1m": DatasetSpec("c4_1m", 1_000_000, 1_000, 1536, 1, 0.0, 0.0, 0.0, 32, 100,
                          (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=4, kind="lowrank",
                          knn="exact_tf32"),
+    # 100M x 100 integers in [-128, 127] from a 5,000-component mixture,
+    # only ever materialised as shards (one per GPU, each built on its own GPU; see materialize_shard_device)
+    "c5_100m": DatasetSpec("c5_100m", 100_000_000, 10_000, 100, 5000, 18.0, -128.0, 127.0, 32, 100,
+                           (128, 256, 512, 1024), seed=5, knn="partitioned", block=500_000),
+    # the same distribution at a tenth of the size (10M rows, 20 blocks): the sharded mode on 2-8 GPUs
+    "c5s_10m": DatasetSpec("c5s_10m", 10_000_000, 10_000, 100, 5000, 18.0, -128.0, 127.0, 32, 100,
+                           (128, 256, 512, 1024), seed=5, knn="partitioned", block=500_000),
     # the headline config's per-component structure (5,000 points per component, degree 32)
     # at a fifth of the size, for profiling captures that must stay small
     "p_200k": DatasetSpec("p_200k", 200_000, 2_000, 128, 40, 25.0, 0.0, 255.0, 32, 100,
                           (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=3),
+    # a blocked spec small enough for tests of the device-built shards
+    "t_blk40k": DatasetSpec("t_blk40k", 40_000, 100, 100, 40, 18.0, -128.0, 127.0, 32, 100,
+                            (128, 256, 512), seed=21, knn="partitioned", block=10_000),
     # small cases for the parity tests (same generators, sizes the oracle finishes in seconds)
     "t_20k": DatasetSpec("t_20k", 20_000, 200, 128, 8, 25.0, 0.0, 255.0, 32, 100,
                          (100, 128, 256, 512, 1024), seed=11),
@@ -161,6 +172,15 @@ def _rng(seed: int, stream: int) -> np.random.Generator:
 def generate_vectors(spec: DatasetSpec) -> Tuple[np.ndarray, np.ndarray]:
     """Base and query vectors (float32) for a spec; deterministic in the seed."""
     return _draw(spec, 1, spec.n), _draw(spec, 2, spec.nq)
+
+
+def generate_block(spec: DatasetSpec, b: int) -> np.ndarray:
+    """Rows [b*block, (b+1)*block) of a blocked spec's base (stream 100 + b):
+    any range of whole blocks can be drawn without the rest of the base."""
+    if spec.block <= 0:
+        raise ValueError(f"{spec.name} is not drawn in blocks")
+    m = min(spec.block, spec.n - b * spec.block)
+    return _draw(spec, 100 + b, m)
 
 
 def generate_queries(spec: DatasetSpec, index: int) -> np.ndarray:
@@ -592,6 +612,271 @@ def build_graph(x: np.ndarray, degree: int, seed: int, knn_k: int = 64, device=N
 
 
 # --------------------------------------------------------------------------
+# device-resident construction (bases of millions of rows)
+# --------------------------------------------------------------------------
+# The same graph recipe as build_graph with knn="partitioned" and the same
+# codes as encode_rows, with every intermediate kept on one GPU (32-bit ids,
+# float32 distances), so that a shard of 12.5M rows needs no host copy of its
+# k-NN lists, candidate lists or codebook.
+def _kmeans_centroids(xt: torch.Tensor, C: int, seed: int, iters: int = 10) -> torch.Tensor:
+    """k-means centroids of a seeded sample of the rows (sums on the host:
+    deterministic)."""
+    n = xt.shape[0]
+    rg = _rng(seed, 11)
+    m = min(n, 64 * C)
+    idx = torch.from_numpy(np.sort(rg.choice(n, size=m, replace=False))).to(xt.device)
+    sample_h = xt[idx].cpu().numpy().astype(np.float32)
+    sample = torch.from_numpy(sample_h).to(xt.device)
+    cent_h = sample_h[rg.choice(m, size=C, replace=False)].astype(np.float64)
+    for _ in range(iters):
+        lab = _nearest_centroid(sample, torch.from_numpy(cent_h.astype(np.float32)).to(xt.device)).cpu().numpy()
+        order = np.argsort(lab, kind="stable")
+        lab_s = lab[order]
+        first = np.concatenate([[0], np.flatnonzero(np.diff(lab_s)) + 1])
+        sums = np.add.reduceat(sample_h[order].astype(np.float64), first, axis=0)
+        cnt = np.diff(np.concatenate([first, [m]]))
+        cent_h[lab_s[first]] = sums / cnt[:, None]
+    return torch.from_numpy(cent_h.astype(np.float32)).to(xt.device)
+
+
+def knn_partitioned_device(xt: torch.Tensor, k: int, seed: int, cluster_size: int = 2048, probe: int = 8,
+                           verbose: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+    """partitioned_knn on a device tensor: (ids int32 [n, k], d2 float32
+    [n, k]) on the same device, ascending, -1 / inf where short."""
+    import time
+    t0 = time.time()
+    dev = xt.device
+    n = xt.shape[0]
+    norms = (xt * xt).sum(1)
+    C = max(1, n // cluster_size)
+    cent = _kmeans_centroids(xt, C, seed)
+    labels = _nearest_centroid(xt, cent)
+    members = torch.argsort(labels, stable=True)
+    counts = torch.bincount(labels, minlength=C)
+    starts = torch.cumsum(counts, 0) - counts
+    del labels
+    cc = (cent * cent).sum(1)
+    cd = cc[:, None] + cc[None, :] - 2.0 * (cent @ cent.T)
+    cd.fill_diagonal_(-1.0)
+    nbr = torch.topk(cd, min(probe, C), dim=1, largest=False).indices.cpu().numpy()
+    counts_h, starts_h = counts.cpu().numpy(), starts.cpu().numpy()
+    if verbose:
+        print(f"[builder] partitioned k-NN: {C} clusters (sizes {counts_h.min()}..{counts_h.max()}), "
+              f"{time.time() - t0:.1f}s", flush=True)
+    out_i = torch.full((n, k), -1, dtype=torch.int32, device=dev)
+    out_d = torch.full((n, k), float("inf"), dtype=torch.float32, device=dev)
+    for c in range(C):
+        if counts_h[c] == 0:
+            continue
+        q = members[starts_h[c]:starts_h[c] + counts_h[c]]
+        pool = torch.cat([members[starts_h[j]:starts_h[j] + counts_h[j]] for j in nbr[c]])
+        d = norms[q][:, None] + norms[pool][None, :] - 2.0 * (xt[q] @ xt[pool].T)
+        d.masked_fill_(q[:, None] == pool[None, :], float("inf"))
+        kk = min(k, pool.numel() - 1)
+        if kk <= 0:
+            continue
+        dv, di = torch.topk(d, kk, dim=1, largest=False, sorted=True)
+        nb = pool[di]
+        dx = ((xt[q][:, None, :] - xt[nb]) ** 2).sum(-1)
+        dx, o = torch.sort(dx, dim=1, stable=True)
+        nb = torch.gather(nb, 1, o)
+        out_i[q, :kk] = torch.where(torch.isinf(torch.gather(dv, 1, o)), torch.full_like(nb, -1), nb).to(torch.int32)
+        out_d[q, :kk] = dx
+    if verbose:
+        print(f"[builder] partitioned k-NN done, {time.time() - t0:.1f}s", flush=True)
+    return out_i, out_d
+
+
+def merge_reverse_device(ids: torch.Tensor, d: torch.Tensor, cap: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """_merge_reverse_large on device tensors: (cand int32 [n, cap], cand_d
+    float32 [n, cap]), -1 / inf where short."""
+    dev = ids.device
+    n, k = ids.shape
+    src = torch.arange(n, device=dev, dtype=torch.int32).repeat_interleave(k)
+    dst = ids.reshape(-1)
+    dd = d.reshape(-1)
+    ok = dst >= 0
+    src, dst, dd = src[ok], dst[ok], dd[ok]
+    node = torch.cat([src, dst])
+    cand = torch.cat([dst, src])
+    dist = torch.cat([dd, dd])
+    del src, dst, dd, ok
+    o = torch.argsort(cand, stable=True)
+    node, cand, dist = node[o], cand[o], dist[o]
+    del o
+    key = (node.to(torch.int64) << 32) | (dist.view(torch.int32).to(torch.int64) & 0xFFFFFFFF)
+    o = torch.argsort(key, stable=True)
+    del key
+    node, cand, dist = node[o], cand[o], dist[o]
+    del o
+    keep = torch.ones_like(node, dtype=torch.bool)
+    keep[1:] = (node[1:] != node[:-1]) | (cand[1:] != cand[:-1])
+    node, cand, dist = node[keep], cand[keep], dist[keep]
+    del keep
+    nl = node.long()
+    del node
+    counts = torch.bincount(nl, minlength=n)
+    starts = torch.cumsum(counts, 0) - counts
+    rank = torch.arange(nl.numel(), device=dev) - starts[nl]
+    sel = rank < cap
+    out_i = torch.full((n, cap), -1, dtype=torch.int32, device=dev)
+    out_d = torch.full((n, cap), float("inf"), dtype=torch.float32, device=dev)
+    out_i[nl[sel], rank[sel]] = cand[sel]
+    out_d[nl[sel], rank[sel]] = dist[sel]
+    return out_i, out_d
+
+
+def rng_prune_device(xt: torch.Tensor, cand: torch.Tensor, cand_d: torch.Tensor, R: int,
+                     alpha: float = 1.0) -> torch.Tensor:
+    """rng_prune on device tensors (float32 pair distances): int32 [n, R]."""
+    dev = xt.device
+    n, C = cand.shape
+    batch = int(min(65536, max(1024, (4 << 30) // (C * (xt.shape[1] + C) * 4))))
+    out = torch.full((n, R), -1, dtype=torch.int32, device=dev)
+    a2 = alpha * alpha
+    pos = torch.arange(C, device=dev)[None, :]
+    for s in range(0, n, batch):
+        e = min(n, s + batch)
+        ci = cand[s:e].long()
+        cd = cand_d[s:e]
+        valid = ci >= 0
+        v = xt[ci.clamp(min=0)]
+        g = v @ v.transpose(1, 2)
+        sq = torch.diagonal(g, dim1=1, dim2=2)
+        pair = (sq[:, :, None] + sq[:, None, :] - 2.0 * g).clamp_(min=0)
+        del v, g
+        B = e - s
+        kept = torch.zeros((B, C), dtype=torch.bool, device=dev)
+        count = torch.zeros(B, dtype=torch.int32, device=dev)
+        for j in range(C):
+            occl = (kept & (pair[:, :, j] * a2 <= cd[:, j:j + 1])).any(1)
+            take = valid[:, j] & ~occl & (count < R)
+            kept[:, j] = take
+            count += take.to(torch.int32)
+        key = torch.where(kept, pos, pos + C)
+        key = torch.where(valid, key, torch.full_like(key, 3 * C))
+        order = torch.argsort(key, dim=1)[:, :R]
+        chosen = torch.gather(ci, 1, order)
+        chosen_valid = torch.gather(valid, 1, order)
+        out[s:e, :chosen.shape[1]] = torch.where(chosen_valid, chosen, torch.full_like(chosen, -1)).to(torch.int32)
+    return out
+
+
+def build_graph_device(xt: torch.Tensor, degree: int, seed: int, knn_k: int = 64,
+                       verbose: bool = False) -> Tuple[torch.Tensor, int]:
+    """build_graph (partitioned k-NN) on a device tensor of the rows:
+    (neighbour lists int32 [n, degree] on the device, -1 = empty; entry)."""
+    import time
+    t0 = time.time()
+    dev = xt.device
+    n = xt.shape[0]
+    k = min(knn_k, n - 1)
+    r = min(max(2, degree // 8), degree - 1)
+    ids, d = knn_partitioned_device(xt, k, seed, verbose=verbose)
+    cand, cand_d = merge_reverse_device(ids, d, cap=min(n - 1, max(96, int(1.5 * k))))
+    del ids, d
+    if verbose:
+        print(f"[builder] reverse edges merged, {time.time() - t0:.1f}s", flush=True)
+    local = rng_prune_device(xt, cand, cand_d, degree - r)
+    del cand, cand_d
+    if verbose:
+        print(f"[builder] pruned, {time.time() - t0:.1f}s", flush=True)
+    rg = _rng(seed, 5)
+    rand = torch.from_numpy(((np.arange(n)[:, None] + 1 + rg.integers(0, max(1, n - 1), size=(n, r))) % n)
+                            .astype(np.int32)).to(dev)
+    nbrs = torch.cat([local, rand], dim=1)
+    del local, rand
+    # a neighbour that repeats an earlier slot of its row becomes an empty slot
+    tri = torch.ones((degree, degree), dtype=torch.bool, device=dev).tril(-1)  # [j, j']: j' < j
+    step = 1 << 20
+    for s0 in range(0, n, step):
+        blk = nbrs[s0:s0 + step]
+        dup = ((blk[:, :, None] == blk[:, None, :]) & tri[None] & (blk[:, None, :] >= 0)).any(2)
+        blk.masked_fill_(dup, -1)
+    # entry: the row nearest the centroid, half of its slots random long edges
+    cen = xt.double().mean(0)
+    best, best_d = 0, float("inf")
+    for s0 in range(0, n, step):
+        dd = ((xt[s0:s0 + step].double() - cen) ** 2).sum(1)
+        v, i = torch.min(dd, 0)
+        if float(v) < best_d:
+            best_d, best = float(v), s0 + int(i)
+    entry = best
+    half = degree // 2
+    extra = (entry + 1 + rg.integers(0, max(1, n - 1), size=half)) % n
+    row = [int(v) for v in nbrs[entry, :degree - r].cpu().tolist() if v >= 0][: degree - half]
+    for v in extra:
+        if int(v) not in row and int(v) != entry:
+            row.append(int(v))
+    row = row[:degree] + [-1] * (degree - min(degree, len(row)))
+    nbrs[entry] = torch.tensor(row, dtype=torch.int32, device=dev)
+    if verbose:
+        print(f"[builder] graph done, {time.time() - t0:.1f}s", flush=True)
+    return nbrs, entry
+
+
+def encode_rows_device(xt: torch.Tensor, nbrs: torch.Tensor, signs: np.ndarray, metric: str = "l2") -> torch.Tensor:
+    """encode_rows on device tensors: the codebook rows float32 [n, row] on
+    the device (the same bytes encode_rows writes)."""
+    dev = xt.device
+    n, dim = xt.shape
+    R = nbrs.shape[1]
+    L = layout(dim, R)
+    D = L.padded_dim
+    rows = torch.zeros((n, L.row), dtype=torch.float32, device=dev)
+    rows[:, :dim] = xt
+    rows_u8 = rows.view(torch.uint8)
+    rows_i32 = rows.view(torch.int32)
+    st = torch.zeros(D, dtype=torch.float64, device=dev)
+    st[:dim] = torch.from_numpy(signs[:dim]).to(dev).double()
+    scale = 2.0 if metric == "l2" else 1.0
+    batch = max(1, (1 << 27) // (R * D))
+    bitw = torch.tensor([8, 4, 2, 1], dtype=torch.int64, device=dev)
+    FMAX = float(FLT_MAX)
+    for s in range(0, n, batch):
+        e = min(n, s + batch)
+        nb = nbrs[s:e].long()
+        valid = nb >= 0
+        c = xt[s:e].double()
+        o = xt[nb.clamp(min=0)].double()
+        diff = o - c[:, None, :]
+        u = torch.zeros((e - s, R, D), dtype=torch.float64, device=dev)
+        u[..., :dim] = diff * st[:dim]
+        u = fwht(u)
+        bits = (u > 0)
+        ip_xu = u.abs().sum(-1)
+        norm_u = u.pow(2).sum(-1)
+        fdq = torch.where(ip_xu > 0, -scale * norm_u / (D * ip_xu), torch.zeros_like(ip_xu))
+        fvq = fdq * (2.0 * bits.sum(-1).double() - D)
+        if metric == "l2":
+            tx = diff.pow(2).sum(-1) + 2.0 * (diff * c[:, None, :]).sum(-1)
+        else:
+            tx = torch.zeros_like(fdq)
+        nib = (bits.view(e - s, R, D // 4, 4).to(torch.int64) * bitw).sum(-1)
+        byte = (nib[..., 0::2] | (nib[..., 1::2] << 4)).to(torch.uint8)
+        tx = torch.where(valid, tx, torch.full_like(tx, FMAX))
+        fdq = torch.where(valid, fdq, torch.zeros_like(fdq))
+        fvq = torch.where(valid, fvq, torch.zeros_like(fvq))
+        byte = torch.where(valid[..., None], byte, torch.zeros_like(byte))
+        rows_u8[s:e, L.code_off * 4: L.code_off * 4 + R * (D // 8)] = byte.reshape(e - s, R * (D // 8))
+        rows[s:e, L.factor_off: L.factor_off + R] = tx.float()
+        rows[s:e, L.factor_off + R: L.factor_off + 2 * R] = fdq.float()
+        rows[s:e, L.factor_off + 2 * R: L.factor_off + 3 * R] = fvq.float()
+        rows_i32[s:e, L.nbr_off: L.nbr_off + R] = torch.where(valid, nb, torch.full_like(nb, -1)).to(torch.int32)
+    return rows
+
+
+def write_codebook_device(path: str, entry: int, rows: torch.Tensor, signs: np.ndarray,
+                          chunk_rows: int = 1 << 20) -> None:
+    """write_codebook from device rows, one chunk of rows at a time."""
+    with open(path, "wb") as f:
+        f.write(struct.pack("<I", entry & 0xFFFFFFFF))
+        for s in range(0, rows.shape[0], chunk_rows):
+            f.write(rows[s:s + chunk_rows].cpu().numpy().tobytes())
+        f.write(np.ascontiguousarray(signs, dtype=np.float32).tobytes())
+
+
+# --------------------------------------------------------------------------
 # RaBitQ encoding
 # --------------------------------------------------------------------------
 def fwht(v: torch.Tensor) -> torch.Tensor:
@@ -752,6 +1037,8 @@ def materialize(name_or_spec, cache_dir: Optional[str] = None, device=None,
         return Dataset(spec, base, queries, gt, rows, signs, entry, L, paths["cb"], d)
     import time
     t0 = time.time()
+    if spec.knn == "partitioned" and spec.n > 2_000_000:
+        return _materialize_on_device(spec, paths, d, L, device, verbose)
     base, queries = generate_vectors(spec)
     if verbose:
         print(f"[builder] {spec.name}: vectors {time.time() - t0:.1f}s", flush=True)
@@ -771,6 +1058,41 @@ def materialize(name_or_spec, cache_dir: Optional[str] = None, device=None,
     write_vecs(paths["query"], queries)
     write_vecs(paths["gt"], gt)
     os.replace(tmp, paths["cb"])
+    if verbose:
+        print(f"[builder] {spec.name}: done {time.time() - t0:.1f}s", flush=True)
+    return Dataset(spec, base, queries, gt, rows, signs, entry, L, paths["cb"], d)
+
+
+def _materialize_on_device(spec: DatasetSpec, paths, d, L, device, verbose) -> Dataset:
+    """materialize for bases of millions of rows: graph and codes built on the
+    GPU (build_graph_device, encode_rows_device), codebook written from the
+    device in chunks, rows returned memory-mapped."""
+    import time
+    t0 = time.time()
+    dev = _device(device)
+    if dev.type != "cuda":
+        raise RuntimeError(f"{spec.name}: {spec.n} rows are built on a GPU only")
+    base, queries = generate_vectors(spec)
+    if verbose:
+        print(f"[builder] {spec.name}: vectors {time.time() - t0:.1f}s", flush=True)
+    xt = torch.from_numpy(base).to(dev)
+    nbrs, entry = build_graph_device(xt, spec.degree, spec.seed, knn_k=spec.knn_k, verbose=verbose)
+    signs = make_signs(L.padded_dim, spec.seed)
+    rows = encode_rows_device(xt, nbrs, signs)
+    del nbrs, xt
+    tmp = paths["cb"] + ".tmp"
+    write_codebook_device(tmp, entry, rows, signs)
+    del rows
+    torch.cuda.empty_cache()
+    if verbose:
+        print(f"[builder] {spec.name}: codes {time.time() - t0:.1f}s", flush=True)
+    gt_ids, _ = brute_force_knn(base, queries, min(spec.gt_k, spec.n), device=device)
+    gt = gt_ids.astype(np.int32)
+    write_vecs(paths["base"], base)
+    write_vecs(paths["query"], queries)
+    write_vecs(paths["gt"], gt)
+    os.replace(tmp, paths["cb"])
+    entry, rows, signs = read_codebook(paths["cb"], spec.n, spec.dim, spec.degree)
     if verbose:
         print(f"[builder] {spec.name}: done {time.time() - t0:.1f}s", flush=True)
     return Dataset(spec, base, queries, gt, rows, signs, entry, L, paths["cb"], d)
@@ -852,3 +1174,61 @@ def materialize_shard(name_or_spec, index: int, count: int, cache_dir: Optional[
         if verbose:
             print(f"[builder] {spec.name} shard {index}/{count}: {e - s} nodes", flush=True)
     return Shard(spec, index, count, s, e - s, full.queries, full.gt, rows, signs, entry, L, cb)
+
+
+@dataclasses.dataclass
+class DeviceShard:
+    """One shard of a blocked spec built on its own GPU (materialize_shard_device)."""
+    spec: DatasetSpec
+    index: int
+    count: int
+    offset: int            # global id of local node 0
+    n: int
+    queries: np.ndarray    # the full query batch
+    rows: torch.Tensor     # float32 [n, row] on the device
+    signs: np.ndarray
+    entry: int
+    layout: Layout
+    gt_ids: np.ndarray     # int64 [nq, gt_k]: this shard's exact nearest rows (global ids)
+    gt_d: np.ndarray       # float64 [nq, gt_k]: their squared distances
+
+
+def materialize_shard_device(name_or_spec, index: int, count: int, device, verbose: bool = False) -> DeviceShard:
+    """Shard `index` of `count` of a blocked spec:
+    its rows (whole blocks, drawn here), its own graph, entry point and codes,
+    built and kept on `device`, plus its exact top-gt_k for every query.  No
+    host ever holds the whole base: the global ground truth is the merge of
+    every shard's lists (merge_shard_ground_truth)."""
+    import time
+    t0 = time.time()
+    spec = SPECS[name_or_spec] if isinstance(name_or_spec, str) else name_or_spec
+    s, e = shard_range(spec.n, count, index)
+    if spec.block <= 0 or s % spec.block or (e % spec.block and e != spec.n):
+        raise ValueError(f"{spec.name}: shard {index} of {count} does not cover whole blocks of {spec.block}")
+    dev = _device(device)
+    base = np.concatenate([generate_block(spec, b) for b in range(s // spec.block, (e + spec.block - 1) // spec.block)])
+    queries = _draw(spec, 2, spec.nq)
+    if verbose:
+        print(f"[builder] {spec.name} shard {index}/{count}: {e - s} rows drawn, {time.time() - t0:.1f}s", flush=True)
+    xt = torch.from_numpy(base).to(dev)
+    nbrs, entry = build_graph_device(xt, spec.degree, spec.seed * 1000 + index, knn_k=spec.knn_k, verbose=verbose)
+    L = layout(spec.dim, spec.degree)
+    signs = make_signs(L.padded_dim, spec.seed)
+    rows = encode_rows_device(xt, nbrs, signs)
+    del nbrs, xt
+    torch.cuda.empty_cache()
+    gi, gd = brute_force_knn(base, queries, min(spec.gt_k, e - s), device=device)
+    if verbose:
+        print(f"[builder] {spec.name} shard {index}/{count}: built, {time.time() - t0:.1f}s", flush=True)
+    return DeviceShard(spec, index, count, s, e - s, queries, rows, signs, entry, L, gi + s, gd)
+
+
+def merge_shard_ground_truth(ids: np.ndarray, d: np.ndarray, k: int) -> np.ndarray:
+    """Global exact top-k from every shard's exact top lists (ids [S, nq, k']
+    global, d [S, nq, k'] squared distances): ordered by (distance, id), as
+    brute_force_knn orders the whole base.  Returns int32 [nq, k]."""
+    S, nq, kk = ids.shape
+    i = ids.transpose(1, 0, 2).reshape(nq, S * kk)
+    dd = d.transpose(1, 0, 2).reshape(nq, S * kk)
+    order = np.lexsort((i, dd), axis=1)[:, :k]
+    return np.take_along_axis(i, order, 1).astype(np.int32)

@@ -385,6 +385,39 @@ int fg_index_create(const float* rows, const float* signs, uint32_t entry, uint6
     return FG_OK;
 }
 
+int fg_index_create_device(const float* d_rows, const float* d_signs, uint32_t entry, uint64_t n, uint64_t dim,
+                           int32_t degree, int32_t metric, int32_t device, fg_index** out) {
+    g_err.clear();
+    if (!out || !d_rows || !d_signs) return fail(FG_ERR_ARG, "null argument");
+    *out = nullptr;
+    int rc = check_shape(n, dim, degree, metric);
+    if (rc) return rc;
+    if (entry >= n) return fail(FG_ERR_ARG, "entry point %u outside [0, %llu)", entry, (unsigned long long)n);
+    if ((rc = check_device(&device))) return rc;
+    auto* x = new fg_index();
+    x->device = device;
+    x->metric = metric;
+    fill_layout(x, n, dim, degree);
+    DeviceGuard g(device);
+    if (g.err != cudaSuccess) {
+        destroy(x);
+        return cuda_fail(g.err, "cudaSetDevice");
+    }
+    if ((rc = alloc_device(x, n))) {
+        destroy(x);
+        return rc;
+    }
+    cudaError_t e = cudaMemcpy(x->d_rows, d_rows, n * x->row * sizeof(float), cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(x->d_signs, d_signs, x->D * sizeof(float), cudaMemcpyDeviceToDevice);
+    if (e != cudaSuccess) {
+        destroy(x);
+        return cuda_fail(e, "cudaMemcpy(codebook, device to device)");
+    }
+    x->entry = entry;
+    *out = x;
+    return FG_OK;
+}
+
 int fg_index_free(fg_index* x) {
     destroy(x);
     return FG_OK;

@@ -84,6 +84,14 @@ int fg_index_load(const char* path, uint64_t num_nodes, uint64_t dim, int32_t de
 int fg_index_create(const float* rows, const float* signs, uint32_t entry_point, uint64_t num_nodes,
                     uint64_t dim, int32_t degree, int32_t metric, int32_t device, fg_index** out);
 
+/* Same, from a codebook already in device memory on `device` (d_rows,
+ * d_signs: device pointers, copied device to device; the caller keeps or
+ * frees its buffers) -- for indexes built on the GPU, such as the shards of
+ * a base too large for one host.  entry_point must be a node id (the
+ * UINT32_MAX centroid fallback needs the rows on the host). */
+int fg_index_create_device(const float* d_rows, const float* d_signs, uint32_t entry_point, uint64_t num_nodes,
+                           uint64_t dim, int32_t degree, int32_t metric, int32_t device, fg_index** out);
+
 /* Replaces ~QuantizationGraph (include/qg.hpp:44-47). NULL is accepted. */
 int fg_index_free(fg_index* index);
 
