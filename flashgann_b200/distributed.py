@@ -130,10 +130,12 @@ def gather_shard_topk(ids: torch.Tensor, dists: torch.Tensor, K: int, offsets, g
     signature) into the global top-K on every rank; `offsets` lists every
     rank's shard offset (global id of its node 0).  Returns (ids int32
     [nq, K] holding uint32 global ids, dists f32 [nq, K])."""
-    world = dist.get_world_size(group)
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
     li = ids.contiguous()
     gd = dists.contiguous()
     nq, k = li.shape
+    if world == 1:  # one shard (a single process): the merge only maps to global ids
+        return merge(li.view(1, nq, k), gd.view(1, nq, k), offsets, K)
     all_i = torch.empty((world * nq, k), dtype=li.dtype, device=li.device)
     all_d = torch.empty((world * nq, k), dtype=gd.dtype, device=gd.device)
     dist.all_gather_into_tensor(all_i, li, group=group)

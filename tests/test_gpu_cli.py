@@ -94,3 +94,19 @@ def test_reference_main_against_the_class_drop_in(name):
         if os.path.exists(REF_EXE):
             ref = _run(REF_EXE, ds, K, beam)
             assert abs(got - ref) <= 100.0 / (len(ds.queries) * K) + 1e-3, f"beam {beam}: {got} vs reference {ref}"
+
+
+def test_cli_on_two_gpus_matches_one():
+    """bin/gpu_flashgann -gpus 2 (the codebook on devices 0 and 1, the batch
+    split between them) prints the one-GPU recall."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one GPU visible")
+    ds = dataset("t_8k16")
+    K, beam = ds.spec.K, 64
+    args = [EXE] + _files(ds) + [str(K), str(beam), str(ds.spec.degree)]
+    one = subprocess.run(args, capture_output=True, text=True, timeout=300)
+    two = subprocess.run(args + ["-gpus", "2"], capture_output=True, text=True, timeout=300)
+    assert one.returncode == 0 and two.returncode == 0, two.stderr[-2000:]
+    pat = r"^Recall@%d: ([0-9.]+)$" % K
+    assert re.search(pat, one.stdout, re.M).group(1) == re.search(pat, two.stdout, re.M).group(1)

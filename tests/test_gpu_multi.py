@@ -51,3 +51,23 @@ def test_multi_rejects_different_indexes():
     finally:
         a.close()
         b.close()
+
+
+def test_multi_spans_distinct_devices_when_there_are_several():
+    """With two or more GPUs visible, the replicas really live on different
+    devices and the stitched result still equals one device's."""
+    import torch
+    import flashgann_b200 as fg
+    ndev = torch.cuda.device_count()
+    if ndev < 2:
+        pytest.skip("one GPU visible")
+    ds = dataset("t_20k")
+    graphs = [_graph("t_20k", device=i) for i in range(ndev)]
+    try:
+        assert sorted(g.device for g in graphs) == list(range(ndev))
+        K, beam = ds.spec.K, 256
+        ids, _, _ = fg.search_multi(graphs, ds.queries, K, beam)
+        assert np.array_equal(ids, graphs[0].search(ds.queries, K, beam))
+    finally:
+        for g in graphs:
+            g.close()
