@@ -102,6 +102,7 @@ class DatasetSpec:
     gt_k: int = 100
     knn: str = "exact"         # graph candidates: exact | exact_tf32 | partitioned (see build_graph)
     block: int = 0             # > 0: the base is drawn in blocks of this many rows, each from a stream of its own
+    random_links: int = -1     # seeded random long edges per node (-1: max(2, degree // 8), see build_graph)
 
 
 SPECS = {
@@ -124,14 +125,14 @@ SPECS = {
     # BASELINE.json configs[3] at full size: 1M x 1536, L2-normalised low-rank model
     "c4_1m": DatasetSpec("c4_1m", 1_000_000, 1_000, 1536, 1, 0.0, 0.0, 0.0, 32, 100,
                          (100, 128, 256, 384, 512, 640, 768, 896, 1024), seed=4, kind="lowrank",
-                         knn="exact_tf32"),
+                         knn="exact_tf32", random_links=0),
     # 100M x 100 integers in [-128, 127] from a 5,000-component mixture,
     # only ever materialised as shards (one per GPU, each built on its own GPU; see materialize_shard_device)
     "c5_100m": DatasetSpec("c5_100m", 100_000_000, 10_000, 100, 5000, 18.0, -128.0, 127.0, 32, 100,
-                           (128, 256, 512, 1024), seed=5, knn="partitioned", block=500_000),
+                           (128, 256, 512, 1024), seed=5, knn="partitioned", block=500_000, random_links=12),
     # the same distribution at a tenth of the size (10M rows, 20 blocks): the sharded mode on 2-8 GPUs
     "c5s_10m": DatasetSpec("c5s_10m", 10_000_000, 10_000, 100, 5000, 18.0, -128.0, 127.0, 32, 100,
-                           (128, 256, 512, 1024), seed=5, knn="partitioned", block=500_000),
+                           (128, 256, 512, 1024), seed=5, knn="partitioned", block=500_000, random_links=12),
     # the headline config's per-component structure (5,000 points per component, degree 32)
     # at a fifth of the size, for profiling captures that must stay small
     "p_200k": DatasetSpec("p_200k", 200_000, 2_000, 128, 40, 25.0, 0.0, 255.0, 32, 100,
@@ -582,8 +583,11 @@ def build_graph(x: np.ndarray, degree: int, seed: int, knn_k: int = 64, device=N
     if verbose:
         print("[builder] pruned", flush=True)
     rg = _rng(seed, 5)
-    rand = (np.arange(n)[:, None] + 1 + rg.integers(0, max(1, n - 1), size=(n, r))) % n
-    nbrs = np.concatenate([local, rand], axis=1)
+    if r:
+        rand = (np.arange(n)[:, None] + 1 + rg.integers(0, max(1, n - 1), size=(n, r))) % n
+        nbrs = np.concatenate([local, rand], axis=1)
+    else:
+        nbrs = local.copy()
     # a random target that repeats an earlier slot becomes an empty slot
     srt = np.sort(nbrs, axis=1)
     if np.any(srt[:, 1:] == srt[:, :-1]):
@@ -763,7 +767,7 @@ def rng_prune_device(xt: torch.Tensor, cand: torch.Tensor, cand_d: torch.Tensor,
 
 
 def build_graph_device(xt: torch.Tensor, degree: int, seed: int, knn_k: int = 64,
-                       verbose: bool = False) -> Tuple[torch.Tensor, int]:
+                       verbose: bool = False, random_links: Optional[int] = None) -> Tuple[torch.Tensor, int]:
     """build_graph (partitioned k-NN) on a device tensor of the rows:
     (neighbour lists int32 [n, degree] on the device, -1 = empty; entry)."""
     import time
@@ -771,7 +775,8 @@ def build_graph_device(xt: torch.Tensor, degree: int, seed: int, knn_k: int = 64
     dev = xt.device
     n = xt.shape[0]
     k = min(knn_k, n - 1)
-    r = min(max(2, degree // 8), degree - 1)
+    r = max(2, degree // 8) if random_links is None or random_links < 0 else random_links
+    r = min(r, degree - 1)
     ids, d = knn_partitioned_device(xt, k, seed, verbose=verbose)
     cand, cand_d = merge_reverse_device(ids, d, cap=min(n - 1, max(96, int(1.5 * k))))
     del ids, d
@@ -782,10 +787,13 @@ def build_graph_device(xt: torch.Tensor, degree: int, seed: int, knn_k: int = 64
     if verbose:
         print(f"[builder] pruned, {time.time() - t0:.1f}s", flush=True)
     rg = _rng(seed, 5)
-    rand = torch.from_numpy(((np.arange(n)[:, None] + 1 + rg.integers(0, max(1, n - 1), size=(n, r))) % n)
-                            .astype(np.int32)).to(dev)
-    nbrs = torch.cat([local, rand], dim=1)
-    del local, rand
+    if r:
+        rand = torch.from_numpy(((np.arange(n)[:, None] + 1 + rg.integers(0, max(1, n - 1), size=(n, r))) % n)
+                                .astype(np.int32)).to(dev)
+        nbrs = torch.cat([local, rand], dim=1)
+        del local, rand
+    else:
+        nbrs = local
     # a neighbour that repeats an earlier slot of its row becomes an empty slot
     tri = torch.ones((degree, degree), dtype=torch.bool, device=dev).tril(-1)  # [j, j']: j' < j
     step = 1 << 20
@@ -1043,7 +1051,7 @@ def materialize(name_or_spec, cache_dir: Optional[str] = None, device=None,
     if verbose:
         print(f"[builder] {spec.name}: vectors {time.time() - t0:.1f}s", flush=True)
     nbrs, entry = build_graph(base, spec.degree, spec.seed, knn_k=spec.knn_k, device=device, knn=spec.knn,
-                              verbose=verbose)
+                              verbose=verbose, random_links=spec.random_links if spec.random_links >= 0 else None)
     if verbose:
         print(f"[builder] {spec.name}: graph {time.time() - t0:.1f}s", flush=True)
     signs = make_signs(L.padded_dim, spec.seed)
@@ -1076,7 +1084,8 @@ def _materialize_on_device(spec: DatasetSpec, paths, d, L, device, verbose) -> D
     if verbose:
         print(f"[builder] {spec.name}: vectors {time.time() - t0:.1f}s", flush=True)
     xt = torch.from_numpy(base).to(dev)
-    nbrs, entry = build_graph_device(xt, spec.degree, spec.seed, knn_k=spec.knn_k, verbose=verbose)
+    nbrs, entry = build_graph_device(xt, spec.degree, spec.seed, knn_k=spec.knn_k, verbose=verbose,
+                                     random_links=spec.random_links)
     signs = make_signs(L.padded_dim, spec.seed)
     rows = encode_rows_device(xt, nbrs, signs)
     del nbrs, xt
@@ -1211,7 +1220,8 @@ def materialize_shard_device(name_or_spec, index: int, count: int, device, verbo
     if verbose:
         print(f"[builder] {spec.name} shard {index}/{count}: {e - s} rows drawn, {time.time() - t0:.1f}s", flush=True)
     xt = torch.from_numpy(base).to(dev)
-    nbrs, entry = build_graph_device(xt, spec.degree, spec.seed * 1000 + index, knn_k=spec.knn_k, verbose=verbose)
+    nbrs, entry = build_graph_device(xt, spec.degree, spec.seed * 1000 + index, knn_k=spec.knn_k, verbose=verbose,
+                                     random_links=spec.random_links)
     L = layout(spec.dim, spec.degree)
     signs = make_signs(L.padded_dim, spec.seed)
     rows = encode_rows_device(xt, nbrs, signs)
