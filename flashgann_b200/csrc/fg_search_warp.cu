@@ -1587,6 +1587,9 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
     // go to the larger CTA
     const void* best = nullptr;
     int best_q = 0;
+    // FG_CTA_WARPS=1|2|4 restricts the CTA size (a tuning knob; results do not depend on it)
+    const char* cw = getenv("FG_CTA_WARPS");
+    const int cta_warps = cw ? atoi(cw) : 0;
     int budgets[2] = {kCtasSmall, kCtasLarge};
     int nbudgets = 2;
     if (mode == kModeStaged) budgets[0] = kCtasStaged, nbudgets = 1;
@@ -1596,6 +1599,7 @@ int plan_search_warp(const SearchArgs& a, SearchPlan* p, int device, char* err, 
         const void* fn = warp_kernel_for(D / 32, p->merge_n2, a.use_ip != 0, minb, mode);
         for (int wpc : {kWarpsPerCta, 2, 1}) {
             if (wpc % warps_per_query) continue;
+            if (cta_warps && wpc != cta_warps) continue;
             const int qpc = wpc / warps_per_query;
             const size_t smem = p->slice_bytes * static_cast<size_t>(qpc);
             if (smem > static_cast<size_t>(max_smem)) continue;
