@@ -826,8 +826,9 @@ int plan_search(const SearchArgs& a, SearchPlan* p, int device, char* err, size_
         const Choice c = kernel_choice(a.nq, device);
         if (c == Choice::kAuto) {
             // the pair mode while the whole batch is resident at once, else one warp per query
+            // (a pair-mode shape that does not fit, e.g. under FG_CTA_WARPS=1, also falls back)
             const int rc = plan_search_warp(a, p, device, err, errlen, 2);
-            if (rc != FG_OK || a.nq <= p->resident_queries) return rc;
+            if (rc == FG_OK && a.nq <= p->resident_queries) return rc;
             return plan_search_warp(a, p, device, err, errlen, 0);
         }
         if (c != Choice::kCta)
