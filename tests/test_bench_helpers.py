@@ -41,3 +41,31 @@ def test_metric_label_names_the_config():
     from flashgann_b200 import builder
     assert b._metric_name(builder.SPECS["c2_1m"]) == "QPS @ recall@100=0.95 (1M x 128, deg 32)"
     assert b._metric_name(builder.SPECS["c1_100k"]) == "QPS @ recall@10=0.95 (100K x 128, deg 16)"
+
+
+def test_calibration_measures_every_beam_and_picks_the_first_reaching_the_target():
+    b = _bench()
+    recalls = {100: 0.5, 256: 0.9, 512: 0.95, 1024: 0.99}
+    calls = []
+
+    def run(beam):
+        calls.append(beam)
+        return beam
+
+    beam, r, table = b._calibrate(run, None, 10, (100, 256, 512, 1024), lambda ids, gt, k: recalls[ids])
+    assert calls == [100, 256, 512, 1024]  # the whole curve, every rank the same calls
+    assert beam == 512 and r == 0.95
+    assert table == [(100, 0.5), (256, 0.9), (512, 0.95), (1024, 0.99)]
+    beam, r, _ = b._calibrate(run, None, 10, (100, 256), lambda ids, gt, k: 0.1)
+    assert beam == 256  # the last beam when none reaches the target
+
+
+def test_workload_config_names_the_split():
+    b = _bench()
+    from flashgann_b200 import builder
+    spec = builder.SPECS["c2_1m"]
+    weak = b._workload_config(spec, 80000, 640, 8, "weak")
+    strong = b._workload_config(spec, 10000, 640, 8, "strong")
+    assert weak["queries_total"] == 80000 and "distinct 10000-query batch per GPU" in weak["parallelism"]
+    assert strong["queries_total"] == 10000 and "split over 8 GPU" in strong["parallelism"]
+    assert set(weak) == set(strong) and "recall" not in " ".join(weak)
