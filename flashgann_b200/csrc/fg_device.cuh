@@ -808,12 +808,6 @@ __device__ __forceinline__ void controller_update(CtlRegs& c, uint32_t beam0, in
     const float e = c.entry_d;
     const float last = finite_lt_max(c.last_d) ? c.last_d : e;
     const float cur = finite_lt_max(c.cur_d) ? c.cur_d : last;
-    float rate = 0.0f;
-    const float denom = fabsf(e);
-    if (isfinite(last) && isfinite(cur) && isfinite(e) && !(denom <= 1.0e-20f)) {
-        const float prog = __fdiv_rn(__fsub_rn(last, cur), denom);
-        if (isfinite(prog) && prog > 0.0f) rate = prog < 1.0f ? prog : 1.0f;
-    }
     c.top1 = top1;
     c.stall = stall;
     c.last_d = last;
@@ -824,6 +818,13 @@ __device__ __forceinline__ void controller_update(CtlRegs& c, uint32_t beam0, in
         c.rho = phase2_rho;
         c.policy_iters += 1;
     } else if (iter == 0 || (iter % CHECK_INTERVAL) == 0) {
+        // expander progress (src/adaptive_search_utils.cuh:51-72), computed only where it is used
+        float rate = 0.0f;
+        const float denom = fabsf(e);
+        if (isfinite(last) && isfinite(cur) && isfinite(e) && !(denom <= 1.0e-20f)) {
+            const float prog = __fdiv_rn(__fsub_rn(last, cur), denom);
+            if (isfinite(prog) && prog > 0.0f) rate = prog < 1.0f ? prog : 1.0f;
+        }
         const float span = phase2_rho > PHASE1_RHO ? __fsub_rn(phase2_rho, PHASE1_RHO) : __fsub_rn(RHO_MAX, RHO_MIN);
         const float base = c.policy_iters == 0 ? PHASE1_RHO : c.rho;
         const float cap = phase2_rho > PHASE1_RHO ? phase2_rho : RHO_MAX;

@@ -468,11 +468,6 @@ __device__ __forceinline__ uint32_t raw_sum_v(const uint32_t (&c)[W], const uint
     return raw;
 }
 
-// L2 prefetch of a row's raw vector (128-byte lines).
-__device__ __forceinline__ void prefetch_row(const float* r, int dim) {
-    for (int l = 0; l < dim; l += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(r + l));
-}
-
 // ------------------------------------------------------------ merge path
 // Merge of the candidate buffer (cidx/cdist[0..cbs)) into the beam
 // (bidx/bdist[0..P)) with the reference's merge-path result
@@ -482,10 +477,50 @@ __device__ __forceinline__ void prefetch_row(const float* r, int dim) {
 // pos[m] == o, else beam[o - #{pos < o}].  Chunks of 32 positions are
 // rewritten from the end, two per step (all reads of a step before its
 // writes; every source index is <= its output, so lower chunks are intact).
+// UNIFORM: chunks past the last landing candidate take the uniform shift
+// first (output o = beam[o - m_in], no per-chunk candidate masks).  Fewer
+// instructions, more code: on a B200 the pair mode (latency-bound, few warps
+// per SM) ran 3.5 % faster with it, the one-warp search at full residency 7 %
+// slower, so only the pair mode uses it.
+template <bool UNIFORM>
 __device__ __forceinline__ void stable_shift(uint32_t* bidx, float* bdist, float k, uint32_t v, uint32_t pos, uint32_t P,
                                              uint32_t p0, int lane) {
     const int first = static_cast<int>(p0 & ~31u);
-    for (int g = static_cast<int>((P - 1) & ~31u); g >= first; g -= 64) {
+    int top = static_cast<int>((P - 1) & ~31u);
+    if constexpr (UNIFORM) {
+        // the candidates that land (pos < P) are lanes 0 .. m_in - 1, positions increasing
+        const int m_in = __popc(__ballot_sync(kFull, pos < P));
+        if (m_in == 0) return;  // the merged beam is the beam
+        const uint32_t pmax = __shfl_sync(kFull, pos, m_in - 1);
+        const int ustop = static_cast<int>((pmax + 32u) & ~31u) > first ? static_cast<int>((pmax + 32u) & ~31u) : first;
+        while (top >= ustop) {
+            const bool two = top - 32 >= ustop;
+            const uint32_t o0 = static_cast<uint32_t>(top) + lane, o1 = o0 - 32u;
+            const bool a0 = o0 < P;
+            float d0 = 0.0f, d1 = 0.0f;
+            uint32_t i0 = 0, i1 = 0;
+            if (a0) {
+                d0 = bdist[o0 - m_in];
+                i0 = bidx[o0 - m_in];
+            }
+            if (two) {
+                d1 = bdist[o1 - m_in];
+                i1 = bidx[o1 - m_in];
+            }
+            __syncwarp();
+            if (a0) {
+                bdist[o0] = d0;
+                bidx[o0] = i0;
+            }
+            if (two) {
+                bdist[o1] = d1;
+                bidx[o1] = i1;
+            }
+            __syncwarp();
+            top -= two ? 64 : 32;
+        }
+    }
+    for (int g = top; g >= first; g -= 64) {
         float od[2];
         uint32_t ov[2];
         bool act[2];
@@ -566,6 +601,7 @@ __device__ __noinline__ void merge_path_ties(uint32_t* s_bidx, float* s_bdist, u
 // The merge path equals the stable merge except at a segment boundary where a
 // beam entry and a candidate tie: those segments are replayed with the
 // reference's splits before the stable shift and written over it.
+template <bool UNIFORM>
 __device__ __forceinline__ uint32_t merge_path_warp(const WSlice& s, uint32_t cbs, uint32_t P, int active, const uint16_t* bnd,
                                     int lane) {
     uint32_t* bidx = s.bidx;
@@ -601,7 +637,7 @@ __device__ __forceinline__ uint32_t merge_path_warp(const WSlice& s, uint32_t cb
             return p0;
         }
     }
-    stable_shift(bidx, bdist, k, v, pos, P, p0, lane);
+    stable_shift<UNIFORM>(bidx, bdist, k, v, pos, P, p0, lane);
     if (nfix > 0) {
         const FixArea f = fix_area(reinterpret_cast<unsigned char*>(s.stage));
         if (lane < 4 * nfix && f.at[lane] != 0xFFFFu) {
@@ -837,7 +873,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
         // merge the previous iteration's candidates (:142-145)
         uint32_t p0 = 0;
         if constexpr (mp) {
-            p0 = merge_path_warp(s, cbs, P, pl.mp_active, bnd, lane);
+            p0 = merge_path_warp<false>(s, cbs, P, pl.mp_active, bnd, lane);
         } else {
             merge_bitonic<MERGE>(bidx, bdist, s.cidx, s.cdist, cbs, iter == 0, lane);
             for (uint32_t i = static_cast<uint32_t>(beam) + lane; i < P; i += 32) {
@@ -879,14 +915,6 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
                 const uint32_t sel = __ballot_sync(kFull, np && i == theta - 1);
                 last_pick = j0 + (__ffs(sel) - 1);
                 num = theta;
-                // prefetch the blocks of the next unexpanded entries of this chunk
-                const uint32_t later = b & ~((sel << 1) - 1u);
-                if ((later >> lane) & 1u) {
-                    const char* blk = reinterpret_cast<const char*>(rows + static_cast<uint64_t>(e & 0x7fffffffu) * rowf +
-                                                                    a.code_off);
-#pragma unroll
-                    for (int l = 0; l < 8; ++l) asm volatile("prefetch.global.L2 [%0];" ::"l"(blk + 128 * l));
-                }
                 break;
             }
             num += __popc(b);
@@ -971,7 +999,6 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
                 const uint32_t r = __popc(ib & lanemask_lt(lane));
                 s.stage[r] = child;
                 s.eslot[r] = lane;
-                prefetch_row(rows + static_cast<uint64_t>(child) * rowf, dim);
             }
             __syncwarp();
             const int ne = __popc(ib);
@@ -1048,7 +1075,6 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
                 if (kl) {
                     const uint32_t r = total + __popc(kb & lanemask_lt(lane));
                     if (r < 32u) s.stage[r] = child;
-                    prefetch_row(rows + static_cast<uint64_t>(child) * rowf, dim);
                 }
                 total += __popc(kb);
                 if constexpr (!STAGED) cur = nxt;
@@ -1076,7 +1102,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
     }
     // final merge (src/adaptive_search.cuh:448-452)
     if constexpr (mp) {
-        merge_path_warp(s, cbs, P, pl.mp_active, bnd, lane);
+        merge_path_warp<false>(s, cbs, P, pl.mp_active, bnd, lane);
     } else {
         merge_bitonic<MERGE>(bidx, bdist, s.cidx, s.cdist, cbs, false, lane);
     }
@@ -1211,7 +1237,7 @@ __device__ __forceinline__ void search_query_pair(const SearchArgs& a, const WPl
             // merge the previous iteration's candidates (:142-145)
             uint32_t p0 = 0;
             if constexpr (mp) {
-                p0 = merge_path_warp(s, cbs, P, pl.mp_active, bnd, lane);
+                p0 = merge_path_warp<true>(s, cbs, P, pl.mp_active, bnd, lane);
             } else {
                 merge_bitonic<MERGE>(bidx, bdist, s.cidx, s.cdist, cbs, iter == 0, lane);
                 for (uint32_t i = static_cast<uint32_t>(beam) + lane; i < P; i += 32) {
@@ -1252,13 +1278,6 @@ __device__ __forceinline__ void search_query_pair(const SearchArgs& a, const WPl
                     const uint32_t sel = __ballot_sync(kFull, np && i == theta - 1);
                     last_pick = j0 + (__ffs(sel) - 1);
                     num = theta;
-                    const uint32_t later = b & ~((sel << 1) - 1u);
-                    if ((later >> lane) & 1u) {
-                        const char* blk = reinterpret_cast<const char*>(rows + static_cast<uint64_t>(e & 0x7fffffffu) * rowf +
-                                                                        a.code_off);
-#pragma unroll
-                        for (int l = 0; l < 8; ++l) asm volatile("prefetch.global.L2 [%0];" ::"l"(blk + 128 * l));
-                    }
                     break;
                 }
                 num += __popc(b);
@@ -1347,7 +1366,6 @@ __device__ __forceinline__ void search_query_pair(const SearchArgs& a, const WPl
                     const uint32_t r = __popc(ib & lanemask_lt(lane));
                     s.stage[r] = child;
                     s.eslot[r] = lane;
-                    prefetch_row(rows + static_cast<uint64_t>(child) * rowf, dim);
                 }
                 __syncwarp();
                 const int ne = __popc(ib);
@@ -1397,10 +1415,7 @@ __device__ __forceinline__ void search_query_pair(const SearchArgs& a, const WPl
                     kl = keep_smallest(est, valid, eff, lane);
                 }
                 const uint32_t kb = __ballot_sync(kFull, kl);
-                if (kl) {
-                    kp[t * 32 + __popc(kb & lanemask_lt(lane))] = child;
-                    prefetch_row(rows + static_cast<uint64_t>(child) * rowf, dim);
-                }
+                if (kl) kp[t * 32 + __popc(kb & lanemask_lt(lane))] = child;
                 if (lane == 0) ctl->kc[t] = __popc(kb);
                 cur = nxt;
             }
@@ -1441,7 +1456,7 @@ __device__ __forceinline__ void search_query_pair(const SearchArgs& a, const WPl
     if (!lead) return;
     // final merge (src/adaptive_search.cuh:448-452)
     if constexpr (mp) {
-        merge_path_warp(s, cbs, P, pl.mp_active, bnd, lane);
+        merge_path_warp<true>(s, cbs, P, pl.mp_active, bnd, lane);
     } else {
         merge_bitonic<MERGE>(bidx, bdist, s.cidx, s.cdist, cbs, false, lane);
     }
