@@ -209,6 +209,12 @@ __device__ __forceinline__ bool w_insert(uint32_t* t, uint32_t slots, uint32_t k
     return false;
 }
 
+// LAST: test a bucket for an empty slot by its last slot alone -- inserts take
+// the first empty slot and nothing is removed between resets, so a bucket
+// with an empty slot has an empty last slot.  On a B200 that was 0.5 %
+// faster in the one-warp search and 0.5 % slower in the pair mode, which
+// keeps the count of empties.
+template <bool LAST>
 __device__ __forceinline__ bool w_contains(const uint32_t* t, uint32_t slots, uint32_t key) {
     const uint32_t nb = slots >> 2;
     uint32_t b1, b2;
@@ -216,7 +222,11 @@ __device__ __forceinline__ bool w_contains(const uint32_t* t, uint32_t slots, ui
     const uint4 v1 = *reinterpret_cast<const uint4*>(t + 4 * b1);
     const uint4 v2 = *reinterpret_cast<const uint4*>(t + 4 * b2);
     if (has_key(v1, key) || has_key(v2, key)) return true;
-    if (empties(v1) || empties(v2) || !(v2.x & kMsb)) return false;
+    if constexpr (LAST) {
+        if (v1.w == kMax || v2.w == kMax || !(v2.x & kMsb)) return false;
+    } else {
+        if (empties(v1) || empties(v2) || !(v2.x & kMsb)) return false;
+    }
     return w_walk_contains(t, nb, key, b2);
 }
 
@@ -953,7 +963,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
             load_parent_pinned<W>(prow, a, static_cast<int>(work), vec, lane, p);
             const bool in_work = static_cast<uint32_t>(lane) < work;
             uint32_t child = p.child;
-            if (child != kMax && (child >= a.n || w_contains(s.hash, slots, child))) child = kMax;
+            if (child != kMax && (child >= a.n || w_contains<true>(s.hash, slots, child))) child = kMax;
             float dist = child == kMax ? FLT_MAX : 0.0f;
             const int keep = keep_for(work, th, rho, false, 0);
             const uint32_t vcount = __popc(__ballot_sync(kFull, in_work && child != kMax));
@@ -1044,7 +1054,7 @@ __device__ __forceinline__ void search_query(const SearchArgs& a, const WPlan& p
                     load_parent_pinned<W>(rows + static_cast<uint64_t>(s.pnode[tn]) * rowf, a, deg, vec, lane, nxt);
                 }
                 const uint32_t child = cur.child;
-                bool valid = child != kMax && child < a.n && !w_contains(s.hash, slots, child);
+                bool valid = child != kMax && child < a.n && !w_contains<true>(s.hash, slots, child);
                 const uint32_t raw_valid = __popc(__ballot_sync(kFull, valid));
                 bool kl;
                 if (keep0 >= static_cast<int>(raw_valid)) {
@@ -1321,7 +1331,7 @@ __device__ __forceinline__ void search_query_pair(const SearchArgs& a, const WPl
                 load_parent_pinned<W>(prow, a, static_cast<int>(work), vec, lane, p);
                 const bool in_work = static_cast<uint32_t>(lane) < work;
                 uint32_t child = p.child;
-                if (child != kMax && (child >= a.n || w_contains(s.hash, slots, child))) child = kMax;
+                if (child != kMax && (child >= a.n || w_contains<false>(s.hash, slots, child))) child = kMax;
                 float dist = child == kMax ? FLT_MAX : 0.0f;
                 const int keep = keep_for(work, th, rho, false, 0);
                 const uint32_t vcount = __popc(__ballot_sync(kFull, in_work && child != kMax));
@@ -1387,7 +1397,7 @@ __device__ __forceinline__ void search_query_pair(const SearchArgs& a, const WPl
                 ParentLane<W> nxt;
                 load_parent_pinned<W>(rows + static_cast<uint64_t>(s.pnode[tn]) * rowf, a, deg, vec, lane, nxt);
                 const uint32_t child = cur.child;
-                bool valid = child != kMax && child < a.n && !w_contains(s.hash, slots, child);
+                bool valid = child != kMax && child < a.n && !w_contains<false>(s.hash, slots, child);
                 const uint32_t raw_valid = __popc(__ballot_sync(kFull, valid));
                 bool kl;
                 if (keep0 >= static_cast<int>(raw_valid)) {
