@@ -295,7 +295,10 @@ def run_flashgann(args, ws, rank, local):
     # Steps alternate between two streams (each with its own output buffer
     # and work counter), so a step's first wave fills the SMs the previous
     # step's last wave leaves idle; the events bracket all of them on the
-    # launching stream.
+    # launching stream.  The planner aims for throughput (batches in flight
+    # on two streams); results do not depend on the kernel it picks.
+    qg.set_plan_goal("throughput")
+    plan = dict(zip(("kernel", "resident_queries"), qg.search_plan(nq, K, beam)))
     side = [torch.cuda.Stream() for _ in range(2)]
     douts = [dout, torch.empty_like(dout)]
 
@@ -351,8 +354,11 @@ def run_flashgann(args, ws, rank, local):
             st_.synchronize()
 
     def synchronous(n):
+        # one call at a time, as the reference is called: the latency plan
+        qg.set_plan_goal("latency")
         for _ in range(n):
             qg.gpu_search_adaptive(nq, hq, K, hres[0], beam)
+        qg.set_plan_goal("throughput")
 
     e2e = {}
     for name, fn in (("streamed", streamed), ("synchronous", synchronous)):
@@ -362,6 +368,8 @@ def run_flashgann(args, ws, rank, local):
         fn(args.steps)
         e2e[name] = _max_over_ranks((time.perf_counter() - t0) / args.steps, ws)
     e2e_ok = bool(np.array_equal(hres[0], hres[1]))
+    qg.set_plan_goal("latency")
+    sync_plan = dict(zip(("kernel", "resident_queries"), qg.search_plan(nq, K, beam)))
     qg.close()
 
     value = total_q / (ms_max / 1e3)
@@ -385,6 +393,8 @@ def run_flashgann(args, ws, rank, local):
         "gpu_launches": args.steps,
         "timing": "device events around all steps; steps alternate between two streams (consecutive "
                   "steps overlap); outputs of both streams identical: %s" % steps_ok,
+        "plan": {"steps_and_streamed_e2e": dict(plan, goal="throughput"),
+                 "synchronous_e2e": dict(sync_plan, goal="latency")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": (traffic["dram_bytes_per_query"] * nq if traffic else None),

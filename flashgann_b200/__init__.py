@@ -116,6 +116,25 @@ class QuantizationGraph:
         _check(lib().fg_index_set_metric(self._h, metric), "fg_index_set_metric")
         self.metric = metric
 
+    def set_plan_goal(self, goal: str) -> None:
+        """What the kernel planner aims for: "latency" (the default: the
+        shortest time of one batch on an idle GPU) or "throughput" (the most
+        queries per second while batches are kept in flight on several
+        streams).  Results do not depend on it (fg_index_set_plan_goal)."""
+        from ._capi import FG_GOAL_LATENCY, FG_GOAL_THROUGHPUT
+        goals = {"latency": FG_GOAL_LATENCY, "throughput": FG_GOAL_THROUGHPUT}
+        if goal not in goals:
+            raise ValueError(f"plan goal must be 'latency' or 'throughput', not {goal!r}")
+        _check(lib().fg_index_set_plan_goal(self._h, goals[goal]), "fg_index_set_plan_goal")
+
+    def search_plan(self, nq: int, K: int, beam: int):
+        """(kernel name, queries resident at once) that a batch of nq queries
+        would run with under the current goal (fg_search_plan)."""
+        from ._capi import FG_PLAN_KERNELS
+        k, r = ctypes.c_int32(-1), ctypes.c_int32(0)
+        _check(lib().fg_search_plan(self._h, nq, K, beam, ctypes.byref(k), ctypes.byref(r)), "fg_search_plan")
+        return FG_PLAN_KERNELS[k.value], r.value
+
     def gpu_search_adaptive(self, nq: int, queries: np.ndarray, K: int, result_idx: np.ndarray,
                             beam_sz: int) -> float:
         """Search nq queries; fills result_idx[nq*K] (uint32) and returns the

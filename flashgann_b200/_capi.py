@@ -21,6 +21,9 @@ FG_ERR_NO_DEVICE = 7
 FG_METRIC_L2 = 0
 FG_METRIC_IP = 1
 FG_ASYNC_SLOTS = 4
+FG_GOAL_LATENCY = 0
+FG_GOAL_THROUGHPUT = 1
+FG_PLAN_KERNELS = {0: "cta", 1: "warp", 2: "staged", 3: "pair"}
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libflashgann.so")
 
@@ -59,6 +62,8 @@ SIGNATURES = [
     ("fg_index_free", ctypes.c_int, [_vp]),
     ("fg_index_layout", ctypes.c_int, [_vp, ctypes.POINTER(Layout)]),
     ("fg_index_set_metric", ctypes.c_int, [_vp, _i32]),
+    ("fg_index_set_plan_goal", ctypes.c_int, [_vp, _i32]),
+    ("fg_search_plan", ctypes.c_int, [_vp, _i32, _i32, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     ("fg_search", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _i32, ctypes.POINTER(_f64)]),
     ("fg_search_noalloc", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _i32, ctypes.POINTER(_f64)]),
     ("fg_search_async", ctypes.c_int, [_vp, _i32, _i32, _vp, _i32, _vp, _i32, _vp]),

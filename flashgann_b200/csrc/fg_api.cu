@@ -25,6 +25,7 @@ struct fg_index {
     int degree = 0;
     uint32_t entry = 0;
     int metric = FG_METRIC_L2;
+    int goal = FG_GOAL_LATENCY;
     float* d_rows = nullptr;
     float* d_signs = nullptr;
     // buffers of the host-buffer search path, grown on demand
@@ -238,6 +239,7 @@ fg::SearchArgs base_args(const fg_index* x) {
     a.degree = x->degree;
     a.entry = x->entry;
     a.use_ip = x->metric == FG_METRIC_IP;
+    a.goal = x->goal;
     a.work_counter = x->d_counter;
     return a;
 }
@@ -443,6 +445,42 @@ int fg_index_set_metric(fg_index* x, int32_t metric) {
     if (!x) return fail(FG_ERR_ARG, "null index");
     if (metric != FG_METRIC_L2 && metric != FG_METRIC_IP) return fail(FG_ERR_ARG, "unknown metric %d", metric);
     x->metric = metric;
+    return FG_OK;
+}
+
+int fg_index_set_plan_goal(fg_index* x, int32_t goal) {
+    if (!x) return fail(FG_ERR_ARG, "null index");
+    if (goal != FG_GOAL_LATENCY && goal != FG_GOAL_THROUGHPUT) return fail(FG_ERR_ARG, "unknown plan goal %d", goal);
+    x->goal = goal;
+    return FG_OK;
+}
+
+int fg_search_plan(fg_index* x, int32_t nq, int32_t K, int32_t beam, int32_t* kernel, int32_t* resident_queries) {
+    g_err.clear();
+    if (!x) return fail(FG_ERR_ARG, "null index");
+    if (nq < 0) return fail(FG_ERR_ARG, "nq must be >= 0 (got %d)", nq);
+    DeviceGuard g(x->device);
+    if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
+    fg::SearchArgs a = base_args(x);
+    a.nq = nq;
+    a.K = K;
+    a.beam = beam;
+    fg::SearchPlan plan;
+    char err[256];
+    const int rc = fg::plan_search(a, &plan, x->device, err, sizeof(err));
+    if (rc) return fail(rc, "%s", err);
+    int k = FG_PLAN_CTA, resident = 0;
+    if (plan.kernel == 1) {
+        k = plan.warp_mode == 1 ? FG_PLAN_STAGED : plan.warp_mode == 2 ? FG_PLAN_PAIR : FG_PLAN_WARP;
+        resident = plan.resident_queries;
+    } else {
+        int sms = 0;
+        cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x->device);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        resident = plan.blocks_per_sm * sms;  // one query per CTA
+    }
+    if (kernel) *kernel = k;
+    if (resident_queries) *resident_queries = resident;
     return FG_OK;
 }
 

@@ -29,6 +29,7 @@ struct SearchArgs {
     uint32_t entry = 0;
     int use_ip = 0;
     int nq = 0, K = 0, beam = 0;
+    int goal = 0;  // FG_GOAL_LATENCY or FG_GOAL_THROUGHPUT: what plan_search optimises for
 };
 
 // Derived per-launch constants, computed on the host (plan_search).

@@ -732,20 +732,27 @@ int variant_from_env() {
 }
 
 // Kernel choice where all apply (padded dim <= 256; they return identical
-// results), by queries per SM, from batch sweeps on a B200: up to 4 the CTA
-// kernel (8 warps per query: the shortest time per query), up to what the
-// pair mode holds resident (10) the warp kernel's pair mode (2 warps per
-// query), above that one warp per query (20 resident queries per SM at beam
-// <= 640 and D = 128).  FG_KERNEL=cta, =pair, =warp or =staged (the warp
-// kernel's staged variant) forces one.
+// results), by queries per SM, from batch sweeps on a B200.  For the
+// shortest time of one batch (FG_GOAL_LATENCY): up to 4 the CTA kernel (8
+// warps per query: the shortest time per query), up to what the pair mode
+// holds resident (10) the warp kernel's pair mode (2 warps per query), above
+// that one warp per query (20 resident queries per SM at beam <= 640 and
+// D = 128).  For batches kept in flight on several streams
+// (FG_GOAL_THROUGHPUT) each batch shares the SMs with the next one: the pair
+// mode while two batches are resident at once, one warp per query above
+// (c2_1m, beam 640, two streams: 592 queries 0.95 ms per batch in the pair
+// mode against 1.36 in the CTA kernel, 1,250 queries 1.45 ms with one warp per
+// query against 1.55 in the pair mode).  FG_KERNEL=cta, =pair, =warp or
+// =staged (the warp kernel's staged variant) forces one.
 enum class Choice { kCta, kWarp, kStaged, kPair, kAuto };
 
-Choice kernel_choice(int nq, int device) {
+Choice kernel_choice(int nq, int device, int goal) {
     const char* v = getenv("FG_KERNEL");
     if (v && v[0] == 'c') return Choice::kCta;
     if (v && v[0] == 'w') return Choice::kWarp;
     if (v && v[0] == 's') return Choice::kStaged;
     if (v && v[0] == 'p') return Choice::kPair;
+    if (goal == FG_GOAL_THROUGHPUT) return Choice::kAuto;
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) sms = 148;
     return nq > 4 * sms ? Choice::kAuto : Choice::kCta;
@@ -823,12 +830,14 @@ int plan_search(const SearchArgs& a, SearchPlan* p, int device, char* err, size_
     const uintptr_t base = reinterpret_cast<uintptr_t>(a.rows);
     p->vec_codes = ((base % 16) == 0 && ((a.row * 4) % 16) == 0 && ((a.code_off * 4) % 16) == 0) ? 1 : 0;
     if (warp_kernel_supports(a.padded_dim)) {
-        const Choice c = kernel_choice(a.nq, device);
+        const Choice c = kernel_choice(a.nq, device, a.goal);
         if (c == Choice::kAuto) {
-            // the pair mode while the whole batch is resident at once, else one warp per query
-            // (a pair-mode shape that does not fit, e.g. under FG_CTA_WARPS=1, also falls back)
+            // the pair mode while the whole batch (two batches, for throughput) is resident at
+            // once, else one warp per query (a pair-mode shape that does not fit, e.g. under
+            // FG_CTA_WARPS=1, also falls back)
             const int rc = plan_search_warp(a, p, device, err, errlen, 2);
-            if (rc == FG_OK && a.nq <= p->resident_queries) return rc;
+            const long long need = a.goal == FG_GOAL_THROUGHPUT ? 2LL * a.nq : static_cast<long long>(a.nq);
+            if (rc == FG_OK && need <= p->resident_queries) return rc;
             return plan_search_warp(a, p, device, err, errlen, 0);
         }
         if (c != Choice::kCta)

@@ -101,6 +101,37 @@ int fg_index_layout(const fg_index* index, fg_layout* out);
 /* Replaces QuantizationGraph::set_metric (include/qg.hpp:54). */
 int fg_index_set_metric(fg_index* index, int32_t metric);
 
+/* What the kernel planner aims for (fg_index_set_plan_goal). */
+#define FG_GOAL_LATENCY 0
+#define FG_GOAL_THROUGHPUT 1
+
+/* Sets what the planner optimises an index's searches for; no counterpart in
+ * the reference (one kernel shape for every batch).  Every kernel returns the
+ * same results, only their speed differs.
+ * FG_GOAL_LATENCY (the default): the shortest time for one batch on an
+ * otherwise idle GPU -- the CTA kernel for batches of up to 4 queries per SM,
+ * the warp kernel's pair mode while the whole batch is resident at once, one
+ * warp per query above.
+ * FG_GOAL_THROUGHPUT: the most queries per second when the caller keeps
+ * batches in flight on two or more streams (fg_search_async, or
+ * fg_search_device on several streams), so that each batch shares the GPU
+ * with the next: the pair mode while two batches of this size are resident at
+ * once, one warp per query above.  FG_KERNEL=cta|pair|warp|staged in the
+ * environment overrides either goal. */
+int fg_index_set_plan_goal(fg_index* index, int32_t goal);
+
+/* Kernel codes of fg_search_plan. */
+#define FG_PLAN_CTA 0    /* one CTA per query */
+#define FG_PLAN_WARP 1   /* one warp per query */
+#define FG_PLAN_STAGED 2 /* one warp per query, parent blocks staged in shared memory */
+#define FG_PLAN_PAIR 3   /* two warps per query */
+
+/* The kernel the planner picks for a batch of nq queries at (K, beam) under
+ * the index's goal, and how many queries it holds resident on the device at
+ * once (kernel and resident_queries may be NULL).  No counterpart in the
+ * reference; launches nothing. */
+int fg_search_plan(fg_index* index, int32_t nq, int32_t K, int32_t beam, int32_t* kernel, int32_t* resident_queries);
+
 /* Replaces QuantizationGraph::gpu_search_adaptive(nq, queries, K, result_idx,
  * beam_sz, elapsed) (gpu_search_adaptive.cu:12-114): host buffers in and out,
  * synchronous.  queries[nq*dim] row-major fp32, result_idx[nq*K].
